@@ -1,0 +1,314 @@
+// C-ABI entry points of libavo_b200_attn.so (declared in include/avo_b200_attn.h).
+//
+// Host responsibilities: validate shapes/alignment the way the reference binding
+// does (candidates/cuda_mma_attention/attention.cpp:13-21 and
+// attention_kernel.cu:180-186: bf16, D == 128, matching shapes), check that the
+// current device is a B200 (compute capability 10.0), build the TMA tensor maps and
+// launch on the caller's stream.  The tensor-map encoder is fetched through
+// cudaGetDriverEntryPoint so the library links no libcuda at build time and loads on
+// machines without a GPU.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <mutex>
+
+#include "attn_fwd.cuh"
+#include "avo_b200_attn.h"
+
+namespace avo_b200 {
+
+// ---------------------------------------------------------------- LSE merge kernels
+// One warp per (head, row): 32 lanes x 4 dims.
+__global__ void lse_merge_kernel(float* __restrict__ acc_o, float* __restrict__ acc_lse,
+                                 const __nv_bfloat16* __restrict__ part_o,
+                                 const float* __restrict__ part_lse, int num_bh, int rows,
+                                 long long po_hs, long long pl_hs) {
+  const long long gw = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= static_cast<long long>(num_bh) * rows) return;
+  const long long h = gw / rows, r = gw % rows;
+  const float la = acc_lse[gw];
+  const float lp = part_lse[h * pl_hs + r];
+  const float lmax = fmaxf(la, lp);
+  float wa = 0.f, wp = 0.f, lnew = -CUDART_INF_F;
+  if (lmax != -CUDART_INF_F) {
+    wa = expf(la - lmax);
+    wp = expf(lp - lmax);
+    const float sum = wa + wp;
+    lnew = lmax + logf(sum);
+    wa /= sum;
+    wp /= sum;
+  }
+  float4* ap = reinterpret_cast<float4*>(acc_o + gw * kHeadDim) + lane;
+  const uint2 raw = *reinterpret_cast<const uint2*>(part_o + h * po_hs + r * kHeadDim + lane * 4);
+  const float2 p01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+  const float2 p23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+  float4 a = *ap;
+  if (wa == 0.f) {
+    a = make_float4(p01.x * wp, p01.y * wp, p23.x * wp, p23.y * wp);
+  } else {
+    a = make_float4(a.x * wa + p01.x * wp, a.y * wa + p01.y * wp, a.z * wa + p23.x * wp,
+                    a.w * wa + p23.y * wp);
+  }
+  *ap = a;
+  if (lane == 0) acc_lse[gw] = lnew;
+}
+
+__global__ void acc_to_bf16_kernel(const float* __restrict__ acc_o, __nv_bfloat16* __restrict__ out,
+                                   int num_bh, int rows, long long out_hs) {
+  const long long gw = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= static_cast<long long>(num_bh) * rows) return;
+  const long long h = gw / rows, r = gw % rows;
+  const float4 a = reinterpret_cast<const float4*>(acc_o + gw * kHeadDim)[lane];
+  uint2 packed;
+  packed.x = pack_bf16x2(a.x, a.y);
+  packed.y = pack_bf16x2(a.z, a.w);
+  *reinterpret_cast<uint2*>(out + h * out_hs + r * kHeadDim + lane * 4) = packed;
+}
+
+// One CTA waits on an mbarrier that is never completed; the bounded wait expires and
+// reports through the status word.  Exercises the watchdog path without a fault.
+__global__ void watchdog_selftest_kernel(int* status, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar_storage;
+  __shared__ int abort_storage;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_addr(&bar_storage), 1);
+    abort_storage = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const Watch w{reinterpret_cast<volatile int*>(&abort_storage), status, limit_ns};
+    (void)wait_phase(smem_addr(&bar_storage), 0, w);
+  }
+  __syncthreads();
+}
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+EncodeTiledFn g_encode = nullptr;
+int g_device_state[kMaxDevices] = {};  // 0 unchecked, 1 ready, -1 not a B200
+
+unsigned long long watchdog_limit_ns() {
+  static const unsigned long long limit = [] {
+    const char* env = std::getenv("AVO_B200_WATCHDOG_MS");
+    long long ms = env ? std::atoll(env) : 0;
+    if (ms <= 0) ms = 2000;
+    return static_cast<unsigned long long>(ms) * 1000000ull;
+  }();
+  return limit;
+}
+
+int resolve_encoder() {
+  if (g_encode != nullptr) return AVO_B200_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult qres = cudaDriverEntryPointSymbolNotFound;
+  const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qres);
+  if (e != cudaSuccess || qres != cudaDriverEntryPointSuccess || fn == nullptr) {
+    (void)cudaGetLastError();
+    return AVO_B200_EDRIVER;
+  }
+  g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  return AVO_B200_OK;
+}
+
+// Checks the current device once (compute capability 10.0) and raises the kernel's
+// dynamic shared-memory limit on it.
+int prepare_device() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) {
+    (void)cudaGetLastError();
+    return AVO_B200_ENODEV;
+  }
+  std::lock_guard<std::mutex> lock(g_mu);
+  const int rc = resolve_encoder();
+  if (rc != AVO_B200_OK) return rc;
+  if (dev < kMaxDevices && g_device_state[dev] == 1) return AVO_B200_OK;
+  if (dev < kMaxDevices && g_device_state[dev] == -1) return AVO_B200_ENODEV;
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return AVO_B200_ENODEV;
+  }
+  if (major != 10 || minor != 0) {
+    if (dev < kMaxDevices) g_device_state[dev] = -1;
+    return AVO_B200_ENODEV;
+  }
+  if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+      cudaSuccess) {
+    (void)cudaGetLastError();
+    return AVO_B200_ELAUNCH;
+  }
+  if (dev < kMaxDevices) g_device_state[dev] = 1;
+  return AVO_B200_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// [heads, rows, 128] bf16 view with `head_stride` elements between heads; TMA box of
+// 64 columns x 128 rows x 1 head, 128-byte swizzle.
+int encode_rows(CUtensorMap* map, const void* base, int rows, int heads, long long head_stride) {
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(heads)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHeadDim) * 2,
+                                 static_cast<cuuint64_t>(head_stride) * 2};
+  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kBlockN), 1};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  const CUresult r =
+      g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+               estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? AVO_B200_OK : AVO_B200_ETENSORMAP;
+}
+
+int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int num_bh,
+               int seq_q, int seq_kv, int head_dim, long long q_hs, long long kv_hs, long long o_hs,
+               long long lse_hs, int causal, float scale, long long q_pos0, long long kv_pos0,
+               int* status, void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr) return AVO_B200_EINVAL;
+  if (head_dim != kHeadDim || num_bh < 0 || seq_q < 0 || seq_kv < 0) return AVO_B200_EINVAL;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return AVO_B200_EINVAL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return AVO_B200_EINVAL;
+  if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u) != 0) return AVO_B200_EINVAL;
+  if (q_hs % 8 != 0 || kv_hs % 8 != 0 || o_hs % 8 != 0) return AVO_B200_EINVAL;
+  if (q_hs < static_cast<long long>(seq_q) * kHeadDim || o_hs < static_cast<long long>(seq_q) * kHeadDim ||
+      kv_hs < static_cast<long long>(seq_kv) * kHeadDim)
+    return AVO_B200_EINVAL;
+  if (lse != nullptr && lse_hs < seq_q) return AVO_B200_EINVAL;
+  if (num_bh == 0 || seq_q == 0) return AVO_B200_OK;
+
+  int rc = prepare_device();
+  if (rc != AVO_B200_OK) return rc;
+
+  const int num_q_blocks = (seq_q + kRowsPerCta - 1) / kRowsPerCta;
+  const long long grid = static_cast<long long>(num_bh) * num_q_blocks;
+  if (grid > INT_MAX) return AVO_B200_EINVAL;
+
+  alignas(64) CUtensorMap tm_q, tm_k, tm_v, tm_o;
+  const int kv_rows = seq_kv > 0 ? seq_kv : 1;  // never read when seq_kv == 0
+  if ((rc = encode_rows(&tm_q, q, seq_q, num_bh, q_hs)) != AVO_B200_OK) return rc;
+  if ((rc = encode_rows(&tm_k, k, kv_rows, num_bh, kv_hs)) != AVO_B200_OK) return rc;
+  if ((rc = encode_rows(&tm_v, v, kv_rows, num_bh, kv_hs)) != AVO_B200_OK) return rc;
+  if ((rc = encode_rows(&tm_o, o, seq_q, num_bh, o_hs)) != AVO_B200_OK) return rc;
+
+  AttnParams p;
+  p.lse = lse;
+  p.status = status;
+  p.lse_head_stride = lse_hs;
+  p.q_pos0 = q_pos0;
+  p.kv_pos0 = kv_pos0;
+  p.watchdog_ns = watchdog_limit_ns();
+  p.seq_q = seq_q;
+  p.seq_kv = seq_kv;
+  p.num_bh = num_bh;
+  p.num_q_blocks = num_q_blocks;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+
+  attn_fwd_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
+      tm_q, tm_k, tm_v, tm_o, p);
+  if (cudaGetLastError() != cudaSuccess) return AVO_B200_ELAUNCH;
+  return AVO_B200_OK;
+}
+
+}  // namespace
+}  // namespace avo_b200
+
+using namespace avo_b200;
+
+extern "C" int avo_b200_abi_version(void) { return 1; }
+
+extern "C" const char* avo_b200_strerror(int code) {
+  switch (code) {
+    case AVO_B200_OK: return "ok";
+    case AVO_B200_EINVAL: return "invalid argument";
+    case AVO_B200_ENODEV: return "current CUDA device is not a B200 (compute capability 10.0)";
+    case AVO_B200_ELAUNCH: return "CUDA launch error";
+    case AVO_B200_ETENSORMAP: return "tensor map encoding failed";
+    case AVO_B200_EDRIVER: return "driver entry point cuTensorMapEncodeTiled unavailable";
+    default: return "unknown error";
+  }
+}
+
+extern "C" int avo_b200_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                                 int batch, int heads, int seq, int head_dim, int causal,
+                                 float softmax_scale, int* status_dev, void* stream) {
+  if (batch < 0 || heads < 0 || seq < 0) return AVO_B200_EINVAL;
+  const long long bh = static_cast<long long>(batch) * heads;
+  if (bh > INT_MAX) return AVO_B200_EINVAL;
+  const long long hs = static_cast<long long>(seq) * kHeadDim;
+  return launch_fwd(q, k, v, o, lse, static_cast<int>(bh), seq, seq, head_dim, hs, hs, hs, seq, causal,
+                    softmax_scale, 0, 0, status_dev, stream);
+}
+
+extern "C" int avo_b200_attn_fwd_block(const void* q, const void* k, const void* v, void* o, float* lse,
+                                       int num_bh, int seq_q, int seq_kv, int head_dim,
+                                       long long q_head_stride, long long kv_head_stride,
+                                       long long o_head_stride, long long lse_head_stride, int causal,
+                                       float softmax_scale, long long q_pos0, long long kv_pos0,
+                                       int* status_dev, void* stream) {
+  return launch_fwd(q, k, v, o, lse, num_bh, seq_q, seq_kv, head_dim, q_head_stride, kv_head_stride,
+                    o_head_stride, lse_head_stride, causal, softmax_scale, q_pos0, kv_pos0, status_dev,
+                    stream);
+}
+
+extern "C" int avo_b200_lse_merge(float* acc_o, float* acc_lse, const void* part_o, const float* part_lse,
+                                  int num_bh, int rows, int head_dim, long long part_o_head_stride,
+                                  long long part_lse_head_stride, void* stream) {
+  if (acc_o == nullptr || acc_lse == nullptr || part_o == nullptr || part_lse == nullptr)
+    return AVO_B200_EINVAL;
+  if (head_dim != kHeadDim || num_bh < 0 || rows < 0) return AVO_B200_EINVAL;
+  if (part_o_head_stride % 4 != 0 || part_o_head_stride < static_cast<long long>(rows) * kHeadDim ||
+      part_lse_head_stride < rows)
+    return AVO_B200_EINVAL;
+  if (!aligned16(acc_o) || (reinterpret_cast<uintptr_t>(part_o) & 7u) != 0) return AVO_B200_EINVAL;
+  const long long warps = static_cast<long long>(num_bh) * rows;
+  if (warps == 0) return AVO_B200_OK;
+  const long long blocks = (warps * 32 + 255) / 256;
+  if (blocks > INT_MAX) return AVO_B200_EINVAL;
+  lse_merge_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      acc_o, acc_lse, reinterpret_cast<const __nv_bfloat16*>(part_o), part_lse, num_bh, rows,
+      part_o_head_stride, part_lse_head_stride);
+  return cudaGetLastError() == cudaSuccess ? AVO_B200_OK : AVO_B200_ELAUNCH;
+}
+
+extern "C" int avo_b200_acc_to_bf16(const float* acc_o, void* out, int num_bh, int rows, int head_dim,
+                                    long long out_head_stride, void* stream) {
+  if (acc_o == nullptr || out == nullptr || head_dim != kHeadDim || num_bh < 0 || rows < 0)
+    return AVO_B200_EINVAL;
+  if (out_head_stride % 4 != 0 || out_head_stride < static_cast<long long>(rows) * kHeadDim)
+    return AVO_B200_EINVAL;
+  if (!aligned16(acc_o) || (reinterpret_cast<uintptr_t>(out) & 7u) != 0) return AVO_B200_EINVAL;
+  const long long warps = static_cast<long long>(num_bh) * rows;
+  if (warps == 0) return AVO_B200_OK;
+  const long long blocks = (warps * 32 + 255) / 256;
+  if (blocks > INT_MAX) return AVO_B200_EINVAL;
+  acc_to_bf16_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      acc_o, reinterpret_cast<__nv_bfloat16*>(out), num_bh, rows, out_head_stride);
+  return cudaGetLastError() == cudaSuccess ? AVO_B200_OK : AVO_B200_ELAUNCH;
+}
+
+extern "C" int avo_b200_watchdog_selftest(int timeout_us, int* status_dev, void* stream) {
+  if (status_dev == nullptr || timeout_us <= 0 || timeout_us > 10000000) return AVO_B200_EINVAL;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return AVO_B200_ENODEV;
+  }
+  watchdog_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      status_dev, static_cast<unsigned long long>(timeout_us) * 1000ull);
+  return cudaGetLastError() == cudaSuccess ? AVO_B200_OK : AVO_B200_ELAUNCH;
+}

@@ -1,0 +1,448 @@
+// BF16 attention forward for sm_100a (B200), head_dim 128.
+//
+// Replaces the candidate kernel behind `attention(q, k, v, causal)` of the AVO
+// candidate contract (candidates/cuda_mma_attention/attention_kernel.cu:22-171 in
+// the reference, a 16x16 WMMA kernel).  The math is the same softmax(QK^T*scale)V
+// with an optional lower-triangular mask (query i sees keys <= i,
+// candidates/cuda_naive_attention/attention_kernel.cu:28) and the online-softmax
+// recurrence of candidates/cuda_tiled_attention/attention_kernel.cu:84-99; the
+// structure is Blackwell-native and shares nothing with the reference kernels:
+//
+//   * one CTA owns 256 query rows of one (batch, head) as two 128-row Q tiles;
+//   * warp 8 streams K and V tiles (128 keys x 128 dims, bf16) with TMA into a
+//     4-slot shared-memory ring (K_j and V_j alternate), mbarrier-tracked;
+//   * warp 9 issues tcgen05.mma: S_i = Q_i K_j^T into TMEM, then O_i += P_i V_j
+//     with P_i read straight from TMEM (it overwrites S_i as bf16);
+//   * warps 0-3 and 4-7 are two softmax warpgroups, one per Q tile, one thread
+//     per query row: tcgen05.ld of the S row, max, exp2 with scale*log2(e) folded
+//     into one FFMA, row sum, tcgen05.st of P.  The running max is only raised
+//     when it grows by more than 2^8 ("conditional rescale"), so O in TMEM is
+//     rescaled rarely; the two groups ping-pong against the tensor core;
+//   * causal tiles above the diagonal are never loaded or multiplied;
+//   * the epilogue scales O by 1/l, stages it (swizzled) in the dead Q buffer and
+//     writes it with a TMA store; LSE (natural log) goes out as coalesced fp32.
+//
+// Every mbarrier wait is bounded by a wall-clock watchdog: on expiry the CTA sets
+// a status bit, stops issuing work, drains its in-flight copies and MMAs, frees
+// TMEM and returns.  Nothing traps.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <math_constants.h>
+
+#include "sm100_ptx.cuh"
+
+namespace avo_b200 {
+
+constexpr int kHeadDim = 128;
+constexpr int kBlockM = 128;                   // rows per Q tile (one M=128 accumulator)
+constexpr int kQTiles = 2;                     // Q tiles per CTA
+constexpr int kRowsPerCta = kBlockM * kQTiles; // 256
+constexpr int kBlockN = 128;                   // keys per K/V tile
+constexpr int kStages = 4;                     // K/V ring depth
+constexpr int kTileBytes = 128 * kHeadDim * 2; // 32 KiB: 128 rows x 128 bf16
+constexpr int kHalfBytes = kTileBytes / 2;     // one 64-column, 128B-swizzled half
+constexpr int kLoadWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 512;            // S0 | S1 | O0 | O1, 128 columns each
+constexpr float kRescaleThreshold = 8.0f;      // log2 units: rescale only past 2^8 growth
+
+// Device status bits (OR-ed into the caller's status word).
+constexpr int kStatusWatchdog = 1;  // a pipeline wait exceeded the watchdog; outputs invalid
+constexpr int kStatusDrain = 2;     // draining in-flight copies/MMAs exceeded the watchdog
+
+// Shared-memory layout, offsets from a 1024-byte aligned base.
+constexpr int kSmemQ = 0;
+constexpr int kSmemRing = kSmemQ + kQTiles * kTileBytes;
+constexpr int kSmemBars = kSmemRing + kStages * kTileBytes;
+enum : int {
+  BAR_Q = 0,
+  BAR_KV_FULL = 1,
+  BAR_KV_EMPTY = BAR_KV_FULL + kStages,
+  BAR_S_FULL = BAR_KV_EMPTY + kStages,
+  BAR_P_READY = BAR_S_FULL + kQTiles,
+  BAR_O_DONE = BAR_P_READY + kQTiles,
+  BAR_DRAIN = BAR_O_DONE + kQTiles,
+  NUM_BARS = BAR_DRAIN + 1
+};
+constexpr int kSmemTmemSlot = kSmemBars + NUM_BARS * 8;
+constexpr int kSmemAbort = kSmemTmemSlot + 4;
+constexpr int kSmemUsed = kSmemAbort + 4;
+constexpr int kSmemBytes = kSmemUsed + 1024;  // slack for the manual 1024-byte alignment
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+
+struct AttnParams {
+  float* lse;                   // [num_bh, lse_head_stride] natural-log LSE, or null
+  int* status;                  // device status word, or null
+  long long lse_head_stride;    // elements between consecutive heads of lse
+  long long q_pos0;             // sequence position of local query row 0 (mask only)
+  long long kv_pos0;            // sequence position of local key row 0 (mask only)
+  unsigned long long watchdog_ns;
+  int seq_q;
+  int seq_kv;
+  int num_bh;
+  int num_q_blocks;             // ceil(seq_q / 256)
+  int causal;                   // key position > query position is masked
+  float scale_log2;             // softmax_scale * log2(e)
+};
+
+struct Watch {
+  volatile int* abort;
+  int* status;
+  unsigned long long limit_ns;
+};
+
+// Waits for completion of phase `parity` of `bar`.  Returns false (and raises the
+// CTA abort flag plus the watchdog status bit) if the limit passes first, or at
+// once if another thread of the CTA already aborted.
+__device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const Watch& w) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*w.abort) return false;
+    if (global_timer_ns() - t0 > w.limit_ns) {
+      *w.abort = 1;
+      if (w.status != nullptr) atomicOr(w.status, kStatusWatchdog);
+      return false;
+    }
+  }
+}
+
+// Bounded wait used only to drain work that is already in flight; ignores the abort flag.
+__device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity, const Watch& w) {
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > w.limit_ns) {
+      if (w.status != nullptr) atomicOr(w.status, kStatusDrain);
+      return;
+    }
+  }
+}
+
+// S = Q K^T for one 128x128 tile: 8 MMAs of K=16 along head_dim.  Both operands are
+// K-major, 128B-swizzled, stored as two 64-column halves of 128 rows.
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_smem, uint32_t k_smem) {
+  constexpr uint32_t idesc = idesc_bf16_f32(kBlockM, kBlockN, 0, 0);
+#pragma unroll
+  for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+    const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+    mma_ss(d_tmem, smem_desc_sw128(q_smem + off, 16, 1024), smem_desc_sw128(k_smem + off, 16, 1024),
+           idesc, kk > 0 ? 1u : 0u);
+  }
+}
+
+// O += P V: P (128 x 128 keys, bf16) from TMEM, V (128 keys x 128 dims) from shared
+// memory as an MN-major operand: dims contiguous, the two 64-dim halves 16 KiB apart
+// (leading byte offset), 8-key groups 1024 B apart (stride byte offset).
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_smem,
+                                         uint32_t accumulate) {
+  constexpr uint32_t idesc = idesc_bf16_f32(kBlockM, kHeadDim, 0, 1);
+#pragma unroll
+  for (int kk = 0; kk < kBlockN / 16; ++kk) {
+    mma_ts(d_tmem, p_tmem + kk * 8, smem_desc_sw128(v_smem + kk * 16 * 128, kHalfBytes, 1024), idesc,
+           (accumulate | (kk > 0 ? 1u : 0u)));
+  }
+}
+
+__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
+__device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                    const AttnParams p) {
+  extern __shared__ uint8_t smem_dyn[];
+  const uint32_t raw = smem_addr(smem_dyn);
+  uint8_t* smem = smem_dyn + ((1024u - (raw & 1023u)) & 1023u);
+  const uint32_t sbase = smem_addr(smem);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  auto bar = [&](int idx) -> uint32_t { return sbase + kSmemBars + idx * 8; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemAbort);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemTmemSlot);
+  const Watch watch{abort_flag, p.status, p.watchdog_ns};
+
+  // Tile coordinates.  Causal grids run the longest query blocks first.
+  int bh, qb;
+  if (p.causal) {
+    qb = p.num_q_blocks - 1 - static_cast<int>(blockIdx.x / p.num_bh);
+    bh = static_cast<int>(blockIdx.x % p.num_bh);
+  } else {
+    bh = static_cast<int>(blockIdx.x / p.num_q_blocks);
+    qb = static_cast<int>(blockIdx.x % p.num_q_blocks);
+  }
+  const int q0 = qb * kRowsPerCta;
+  const int n_kv_total = (p.seq_kv + kBlockN - 1) / kBlockN;
+  int n_tiles = n_kv_total;
+  if (p.causal) {
+    const long long q_last = p.q_pos0 + min(q0 + kRowsPerCta, p.seq_q) - 1;
+    const long long lim = q_last - p.kv_pos0;  // largest local key index any row may see
+    n_tiles = lim < 0 ? 0 : static_cast<int>(min(static_cast<long long>(n_kv_total), lim / kBlockN + 1));
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(BAR_Q), 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(BAR_KV_FULL + s), 1);
+      mbar_init(bar(BAR_KV_EMPTY + s), 1);
+    }
+    for (int i = 0; i < kQTiles; ++i) {
+      mbar_init(bar(BAR_S_FULL + i), 1);
+      mbar_init(bar(BAR_P_READY + i), kBlockM);
+      mbar_init(bar(BAR_O_DONE + i), 1);
+    }
+    mbar_init(bar(BAR_DRAIN), 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == kLoadWarp && lane == 0) {
+    prefetch_tensormap(&tm_q);
+    prefetch_tensormap(&tm_k);
+    prefetch_tensormap(&tm_v);
+    prefetch_tensormap(&tm_o);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_addr(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const uint32_t sQ = sbase + kSmemQ;
+  const uint32_t sRing = sbase + kSmemRing;
+
+  if (warp < 2 * 4) {
+    // ------------------------------------------------------------ softmax warpgroups
+    const int i = warp >> 2;          // Q tile of this warpgroup
+    const int wq = warp & 3;          // TMEM lane quarter of this warp
+    const int t = threadIdx.x & 127;  // row within the Q tile
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_off + i * kBlockN;
+    const uint32_t tO = tmem + lane_off + 2 * kBlockN + i * kHeadDim;
+    const int row = q0 + i * kBlockM + t;
+    const long long qpos = p.q_pos0 + row;
+    const long long warp_qpos_min = p.q_pos0 + q0 + i * kBlockM + wq * 32;
+    const float scale = p.scale_log2;
+
+    float m = -CUDART_INF_F;  // running max, log2 units (already scaled)
+    float l = 0.f;            // running sum of exp2(s*scale - m)
+    bool ok = true;
+
+    for (int j = 0; j < n_tiles; ++j) {
+      ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_S_FULL + i), j & 1, watch));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t s[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_wait_ld(s[c]);
+
+      const int key_base = j * kBlockN;
+      const bool tail = key_base + kBlockN > p.seq_kv;
+      const bool diag = p.causal && (p.kv_pos0 + key_base + kBlockN - 1 > warp_qpos_min);
+      if (tail || diag) {
+        long long lim = p.seq_kv - key_base;
+        if (p.causal) lim = min(lim, qpos - (p.kv_pos0 + key_base) + 1);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e >= lim) s[c][e] = f2u(-CUDART_INF_F);
+      }
+
+      float mx[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx[e] = -CUDART_INF_F;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx[e & 7] = fmaxf(mx[e & 7], u2f(s[c][e]));
+      float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                       fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float m_new = fmaxf(m, mt * scale);
+      const bool grow = m_new > m + kRescaleThreshold;
+      float factor = 1.f;
+      if (grow) {
+        factor = ex2_approx(m - m_new);
+        l *= factor;
+        m = m_new;
+      }
+      const float neg_m = (m == -CUDART_INF_F) ? 0.f : -m;
+
+      uint32_t pk[2][32];
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float p0 = ex2_approx(fmaf(u2f(s[c][e]), scale, neg_m));
+          const float p1 = ex2_approx(fmaf(u2f(s[c][e + 1]), scale, neg_m));
+          rs[(e >> 1) & 3] += p0 + p1;
+          pk[c >> 1][(c & 1) * 16 + (e >> 1)] = pack_bf16x2(p0, p1);
+        }
+      }
+      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+      tmem_st32(tS + 0, pk[0]);
+      tmem_st32(tS + 32, pk[1]);
+
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // O holds P V summed over tiles < j relative to the old max: wait for the
+        // last of those MMAs, then rescale this row in TMEM.
+        ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (j - 1) & 1, watch));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld(o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = f2u(u2f(o[e]) * factor);
+          tmem_st32(tO + c * 32, o);
+        }
+      }
+      tc_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(BAR_P_READY + i));
+    }
+
+    if (ok && n_tiles > 0) {
+      ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (n_tiles - 1) & 1, watch));
+      tc_fence_after();
+    }
+
+    // Epilogue: O / l -> bf16 -> swizzled stage in this tile's (now idle) Q buffer.
+    const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+    uint8_t* stage = smem + kSmemQ + i * kTileBytes;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t o[32];
+      if (ok && n_tiles > 0) {
+        tmem_ld32(tO + c * 32, o);
+        tmem_wait_ld(o);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = 0u;
+      }
+      uint8_t* rowp = stage + (c >> 1) * kHalfBytes + t * 128;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 v;
+        v.x = pack_bf16x2(u2f(o[8 * q + 0]) * inv_l, u2f(o[8 * q + 1]) * inv_l);
+        v.y = pack_bf16x2(u2f(o[8 * q + 2]) * inv_l, u2f(o[8 * q + 3]) * inv_l);
+        v.z = pack_bf16x2(u2f(o[8 * q + 4]) * inv_l, u2f(o[8 * q + 5]) * inv_l);
+        v.w = pack_bf16x2(u2f(o[8 * q + 6]) * inv_l, u2f(o[8 * q + 7]) * inv_l);
+        const int chunk = ((c & 1) * 4 + q) ^ (t & 7);
+        *reinterpret_cast<uint4*>(rowp + chunk * 16) = v;
+      }
+    }
+    if (p.lse != nullptr && row < p.seq_q) {
+      const float lse = (l > 0.f) ? (m + log2f(l)) * 0.69314718055994531f : -CUDART_INF_F;
+      p.lse[static_cast<long long>(bh) * p.lse_head_stride + row] = lse;
+    }
+    fence_proxy_async_smem();
+    named_bar_sync(1 + i, 128);
+    if (t == 0 && *abort_flag == 0) {
+      const uint32_t st = sQ + i * kTileBytes;
+      tma_store_3d(&tm_o, st, 0, q0 + i * kBlockM, bh);
+      tma_store_3d(&tm_o, st + kHalfBytes, 64, q0 + i * kBlockM, bh);
+      bulk_commit_group();
+      bulk_wait_group_read0();
+    }
+  } else if (warp == kLoadWarp) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && n_tiles > 0) {
+      const uint64_t pol_q = policy_evict_first();
+      const uint64_t pol_kv = policy_evict_last();
+      mbar_arrive_expect_tx(bar(BAR_Q), kQTiles * kTileBytes);
+      for (int i = 0; i < kQTiles; ++i)
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d(sQ + i * kTileBytes + h * kHalfBytes, &tm_q, bar(BAR_Q), h * 64, q0 + i * kBlockM, bh,
+                      pol_q);
+      int issued = 0;
+      for (int tt = 0; tt < 2 * n_tiles; ++tt) {
+        const int slot = tt % kStages;
+        const int use = tt / kStages;
+        if (use > 0 && !wait_phase(bar(BAR_KV_EMPTY + slot), (use - 1) & 1, watch)) break;
+        mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), kTileBytes);
+        const CUtensorMap* tm = (tt & 1) ? &tm_v : &tm_k;
+        const int krow = (tt >> 1) * kBlockN;
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d(sRing + slot * kTileBytes + h * kHalfBytes, tm, bar(BAR_KV_FULL + slot), h * 64, krow,
+                      bh, pol_kv);
+        issued = tt + 1;
+      }
+      if (*abort_flag) {
+        // Copies already issued still land in shared memory: wait for them.  Slot s
+        // last received copy number s + kStages * ((issued - 1 - s) / kStages).
+        drain_phase(bar(BAR_Q), 0, watch);
+        for (int s = 0; s < kStages; ++s)
+          if (issued > s) drain_phase(bar(BAR_KV_FULL + s), ((issued - 1 - s) / kStages) & 1, watch);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_tiles > 0) {
+      const uint32_t tS0 = tmem, tS1 = tmem + kBlockN;
+      const uint32_t tO0 = tmem + 2 * kBlockN, tO1 = tO0 + kHeadDim;
+      const uint32_t sQ0 = sQ, sQ1 = sQ + kTileBytes;
+      bool ok = wait_phase(bar(BAR_Q), 0, watch) && wait_phase(bar(BAR_KV_FULL + 0), 0, watch);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(tS0, sQ0, sRing);
+        mma_commit(bar(BAR_S_FULL + 0));
+        issue_qk(tS1, sQ1, sRing);
+        mma_commit(bar(BAR_S_FULL + 1));
+        mma_commit(bar(BAR_KV_EMPTY + 0));
+      }
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int tv = 2 * j + 1, sv = tv % kStages;
+        const int tk = 2 * j + 2, sk = tk % kStages;
+        const bool more = j + 1 < n_tiles;
+        const uint32_t v_smem = sRing + sv * kTileBytes;
+        const uint32_t k_smem = sRing + sk * kTileBytes;
+        if (!wait_phase(bar(BAR_KV_FULL + sv), (tv / kStages) & 1, watch)) break;
+        if (!wait_phase(bar(BAR_P_READY + 0), j & 1, watch)) break;
+        tc_fence_after();
+        issue_pv(tO0, tS0, v_smem, j > 0 ? 1u : 0u);
+        mma_commit(bar(BAR_O_DONE + 0));
+        if (more) {
+          if (!wait_phase(bar(BAR_KV_FULL + sk), (tk / kStages) & 1, watch)) break;
+          tc_fence_after();
+          issue_qk(tS0, sQ0, k_smem);
+          mma_commit(bar(BAR_S_FULL + 0));
+        }
+        if (!wait_phase(bar(BAR_P_READY + 1), j & 1, watch)) break;
+        tc_fence_after();
+        issue_pv(tO1, tS1, v_smem, j > 0 ? 1u : 0u);
+        mma_commit(bar(BAR_O_DONE + 1));
+        mma_commit(bar(BAR_KV_EMPTY + sv));
+        if (more) {
+          issue_qk(tS1, sQ1, k_smem);
+          mma_commit(bar(BAR_S_FULL + 1));
+          mma_commit(bar(BAR_KV_EMPTY + sk));
+        }
+      }
+      // Every MMA issued above completes before TMEM and shared memory are released.
+      mma_commit(bar(BAR_DRAIN));
+      drain_phase(bar(BAR_DRAIN), 0, watch);
+    }
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace avo_b200

@@ -1,0 +1,277 @@
+"""ctypes binding to libavo_b200_attn.so, the sm_100a attention-forward library.
+
+This is the host side of the candidate behind the AVO contract
+``attention(q, k, v, causal)`` (reference: candidates/torch_sdpa_seed.py:6-7, the
+loader avo/benchmark.py:406-418).  It restates the reference binding's argument
+checks (candidates/cuda_mma_attention/attention.cpp:13-21: CUDA, contiguous,
+equal shapes, rank 4; attention_kernel.cu:180-186: bf16, head_dim 128) and raises
+``RuntimeError`` subclasses with the same meaning, then calls the C ABI declared in
+include/avo_b200_attn.h on the tensors' current CUDA stream.
+
+There is no fallback: if the library cannot be built or loaded, or the device is
+not a B200, every call raises.  PyTorch is used only for device memory and streams.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import importlib.util
+import math
+import sys
+import threading
+from pathlib import Path
+from typing import Any
+
+HERE = Path(__file__).resolve().parent
+
+# Every function declared in include/avo_b200_attn.h, with (restype, argtypes).
+_c_int, _c_ll, _c_float, _vp = ctypes.c_int, ctypes.c_longlong, ctypes.c_float, ctypes.c_void_p
+SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
+    "avo_b200_abi_version": (_c_int, []),
+    "avo_b200_strerror": (ctypes.c_char_p, [_c_int]),
+    "avo_b200_attn_fwd": (
+        _c_int,
+        [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _vp, _vp],
+    ),
+    "avo_b200_attn_fwd_block": (
+        _c_int,
+        [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
+         _c_ll, _c_ll, _c_ll, _c_ll, _c_int, _c_float, _c_ll, _c_ll, _vp, _vp],
+    ),
+    "avo_b200_lse_merge": (
+        _c_int,
+        [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_ll, _c_ll, _vp],
+    ),
+    "avo_b200_acc_to_bf16": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_ll, _vp]),
+    "avo_b200_watchdog_selftest": (_c_int, [_c_int, _vp, _vp]),
+}
+ABI_VERSION = 1
+HEAD_DIM = 128
+STATUS_WATCHDOG = 1
+STATUS_DRAIN = 2
+
+
+class B200AttentionError(RuntimeError):
+    """A C-ABI call returned a non-zero code, or the device reported a watchdog abort."""
+
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+_status_words: dict[int, Any] = {}
+
+
+def _build_module():
+    name = "avo_b200_attention_build"
+    module = sys.modules.get(name)
+    if module is None:
+        spec = importlib.util.spec_from_file_location(name, HERE / "build.py")
+        module = importlib.util.module_from_spec(spec)
+        sys.modules[name] = module
+        spec.loader.exec_module(module)
+    return module
+
+
+def library_path() -> Path:
+    return _build_module().LIB_PATH
+
+
+def load_library(*, build: bool = True) -> ctypes.CDLL:
+    """Load (building first if missing or stale, when ``build``) the C-ABI library."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        builder = _build_module()
+        if build:
+            builder.build()
+        path = builder.LIB_PATH
+        if not path.is_file():
+            raise B200AttentionError(f"{path} is missing; run build.py")
+        lib = ctypes.CDLL(str(path))
+        for symbol, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, symbol)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        version = lib.avo_b200_abi_version()
+        if version != ABI_VERSION:
+            raise B200AttentionError(f"ABI version {version} != expected {ABI_VERSION}")
+        _lib = lib
+        return lib
+
+
+def strerror(code: int) -> str:
+    return load_library().avo_b200_strerror(code).decode()
+
+
+def _check(code: int, what: str) -> None:
+    if code != 0:
+        raise B200AttentionError(f"{what} failed: {strerror(code)} (code {code})")
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _stream_handle(device) -> int:
+    return _torch().cuda.current_stream(device).cuda_stream
+
+
+def status_word(device) -> Any:
+    """Per-device int32 word that kernels OR their watchdog bits into."""
+    torch = _torch()
+    index = torch.device(device).index
+    if index is None:
+        index = torch.cuda.current_device()
+    word = _status_words.get(index)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=f"cuda:{index}")
+        _status_words[index] = word
+    return word
+
+
+def check_status(device, *, reset: bool = True) -> int:
+    """Synchronize ``device``'s status word; raise if a kernel reported an abort."""
+    word = status_word(device)
+    value = int(word.item())
+    if reset and value:
+        word.zero_()
+    if value & (STATUS_WATCHDOG | STATUS_DRAIN):
+        raise B200AttentionError(
+            f"device watchdog fired (status {value}): a kernel pipeline wait timed out; "
+            "outputs of that launch are invalid"
+        )
+    return value
+
+
+def _validate(q, k, v) -> None:
+    torch = _torch()
+    # Same checks, same order, as the reference binding (attention.cpp:13-21).
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not t.is_contiguous():
+            raise RuntimeError(f"{name} must be contiguous")
+    if q.shape != k.shape:
+        raise RuntimeError("q and k must have the same shape")
+    if q.shape != v.shape:
+        raise RuntimeError("q and v must have the same shape")
+    if q.dim() != 4:
+        raise RuntimeError("q, k, and v must have shape (batch, heads, seq, dim)")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.dtype != torch.bfloat16:
+            raise RuntimeError(f"{name} must be bf16")
+    if q.shape[3] != HEAD_DIM:
+        raise RuntimeError("head_dim must be 128")
+    if not (q.device == k.device == v.device):
+        raise RuntimeError("q, k, and v must be on the same device")
+
+
+def default_scale(head_dim: int = HEAD_DIM) -> float:
+    return 1.0 / math.sqrt(head_dim)
+
+
+def attention_forward(q, k, v, causal: bool, *, softmax_scale: float | None = None,
+                      need_lse: bool = True, out=None, lse=None):
+    """O (bf16, like q) and LSE (fp32 [B, H, S], natural log, or None) of SDPA."""
+    torch = _torch()
+    _validate(q, k, v)
+    batch, heads, seq, head_dim = (int(x) for x in q.shape)
+    if out is None:
+        out = torch.empty_like(q)
+    if need_lse and lse is None:
+        lse = torch.empty((batch, heads, seq), dtype=torch.float32, device=q.device)
+    if not need_lse:
+        lse = None
+    scale = default_scale(head_dim) if softmax_scale is None else float(softmax_scale)
+    lib = load_library()
+    with torch.cuda.device(q.device):
+        code = lib.avo_b200_attn_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+            lse.data_ptr() if lse is not None else None,
+            batch, heads, seq, head_dim, 1 if causal else 0, scale,
+            status_word(q.device).data_ptr(), _stream_handle(q.device),
+        )
+    _check(code, "avo_b200_attn_fwd")
+    return out, lse
+
+
+def attention_block(q, k, v, out, lse, *, causal: bool, q_pos0: int, kv_pos0: int,
+                    softmax_scale: float | None = None) -> None:
+    """Block attention on [num_bh, rows, 128] views (rows contiguous, any head stride).
+
+    ``q``/``out`` are [num_bh, seq_q, 128] bf16, ``k``/``v`` [num_bh, seq_kv, 128] bf16,
+    ``lse`` fp32 [num_bh, seq_q] (row-contiguous); positions drive the causal mask.
+    """
+    torch = _torch()
+    for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
+        if t.dim() != 3 or t.shape[2] != HEAD_DIM or t.stride(2) != 1 or t.stride(1) != HEAD_DIM:
+            raise RuntimeError(f"{name} must be [num_bh, rows, 128] with contiguous rows")
+        if t.dtype != torch.bfloat16:
+            raise RuntimeError(f"{name} must be bf16")
+    if k.stride(0) != v.stride(0) or k.shape != v.shape:
+        raise RuntimeError("k and v must share shape and head stride")
+    if lse is not None and (lse.dim() != 2 or lse.stride(1) != 1 or lse.dtype != torch.float32):
+        raise RuntimeError("lse must be fp32 [num_bh, seq_q] with contiguous rows")
+    num_bh, seq_q, _ = (int(x) for x in q.shape)
+    seq_kv = int(k.shape[1])
+    scale = default_scale() if softmax_scale is None else float(softmax_scale)
+    lib = load_library()
+    with torch.cuda.device(q.device):
+        code = lib.avo_b200_attn_fwd_block(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+            lse.data_ptr() if lse is not None else None,
+            num_bh, seq_q, seq_kv, HEAD_DIM,
+            q.stride(0), k.stride(0), out.stride(0), lse.stride(0) if lse is not None else seq_q,
+            1 if causal else 0, scale, int(q_pos0), int(kv_pos0),
+            status_word(q.device).data_ptr(), _stream_handle(q.device),
+        )
+    _check(code, "avo_b200_attn_fwd_block")
+
+
+def lse_merge(acc_o, acc_lse, part_o, part_lse) -> None:
+    """Fold one partial (bf16 O, fp32 LSE) into fp32 accumulators by log-sum-exp."""
+    torch = _torch()
+    num_bh, rows, head_dim = (int(x) for x in acc_o.shape)
+    if not acc_o.is_contiguous() or acc_o.dtype != torch.float32:
+        raise RuntimeError("acc_o must be contiguous fp32 [num_bh, rows, 128]")
+    if not acc_lse.is_contiguous() or acc_lse.dtype != torch.float32:
+        raise RuntimeError("acc_lse must be contiguous fp32 [num_bh, rows]")
+    if part_o.stride(2) != 1 or part_o.stride(1) != HEAD_DIM or part_o.dtype != torch.bfloat16:
+        raise RuntimeError("part_o must be bf16 [num_bh, rows, 128] with contiguous rows")
+    lib = load_library()
+    with torch.cuda.device(acc_o.device):
+        code = lib.avo_b200_lse_merge(
+            acc_o.data_ptr(), acc_lse.data_ptr(), part_o.data_ptr(), part_lse.data_ptr(),
+            num_bh, rows, head_dim, part_o.stride(0), part_lse.stride(0),
+            _stream_handle(acc_o.device),
+        )
+    _check(code, "avo_b200_lse_merge")
+
+
+def acc_to_bf16(acc_o, out) -> None:
+    torch = _torch()
+    num_bh, rows, head_dim = (int(x) for x in acc_o.shape)
+    if out.stride(2) != 1 or out.stride(1) != HEAD_DIM or out.dtype != torch.bfloat16:
+        raise RuntimeError("out must be bf16 [num_bh, rows, 128] with contiguous rows")
+    lib = load_library()
+    with torch.cuda.device(acc_o.device):
+        code = lib.avo_b200_acc_to_bf16(
+            acc_o.data_ptr(), out.data_ptr(), num_bh, rows, head_dim, out.stride(0),
+            _stream_handle(acc_o.device),
+        )
+    _check(code, "avo_b200_acc_to_bf16")
+
+
+def watchdog_selftest(device, timeout_us: int = 20000) -> int:
+    """Run the never-completing-wait kernel; returns the status bits it reported."""
+    torch = _torch()
+    word = torch.zeros(1, dtype=torch.int32, device=device)
+    lib = load_library()
+    with torch.cuda.device(word.device):
+        code = lib.avo_b200_watchdog_selftest(int(timeout_us), word.data_ptr(),
+                                              _stream_handle(word.device))
+    _check(code, "avo_b200_watchdog_selftest")
+    return int(word.item())

@@ -1,0 +1,114 @@
+/*
+ * avo_b200_attn.h - C ABI of the B200 (sm_100a) attention-forward library
+ * libavo_b200_attn.so.
+ *
+ * The AVO candidate contract is the Python callable `attention(q, k, v, causal)`
+ * (reference: candidates/torch_sdpa_seed.py:6-7, loaded and checked by
+ * avo/benchmark.py:406-418); the reference's CUDA seeds reach their kernels through
+ * a pybind11 binding `attention(q, k, v, causal)` that TORCH_CHECKs its tensors and
+ * calls `attention_cuda` (candidates/cuda_mma_attention/attention.cpp:8-26,
+ * candidates/cuda_mma_attention/attention_kernel.cu:175-206).  This header is the
+ * replacement boundary: plain pointers and sizes, no torch types.  Tensors are
+ * caller-owned device memory; nothing here allocates device memory; every launch is
+ * asynchronous on `stream` (a cudaStream_t, 0 = legacy default stream).
+ *
+ * Layout: q, k, v, o are bf16 [batch, heads, seq, 128] contiguous (the SDPA layout);
+ * lse is fp32 [batch, heads, seq], natural log of sum_j exp(scale * q.k_j).
+ *
+ * Return codes (host side, synchronous):
+ *   AVO_B200_OK                0
+ *   AVO_B200_EINVAL            1  bad argument (shape, alignment, null pointer, scale)
+ *   AVO_B200_ENODEV            2  current device is not compute capability 10.0 (B200)
+ *   AVO_B200_ELAUNCH           3  CUDA reported an error at launch
+ *   AVO_B200_ETENSORMAP        4  cuTensorMapEncodeTiled rejected a descriptor
+ *   AVO_B200_EDRIVER           5  driver entry point for tensor maps unavailable
+ *
+ * Device status bits (written asynchronously into *status_dev when non-null; the
+ * caller zeroes the word and reads it after synchronizing):
+ *   AVO_B200_STATUS_WATCHDOG   1  a pipeline wait exceeded the watchdog; outputs invalid
+ *   AVO_B200_STATUS_DRAIN      2  draining in-flight work after an abort also timed out
+ */
+#ifndef AVO_B200_ATTN_H_
+#define AVO_B200_ATTN_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AVO_B200_OK 0
+#define AVO_B200_EINVAL 1
+#define AVO_B200_ENODEV 2
+#define AVO_B200_ELAUNCH 3
+#define AVO_B200_ETENSORMAP 4
+#define AVO_B200_EDRIVER 5
+
+#define AVO_B200_STATUS_WATCHDOG 1
+#define AVO_B200_STATUS_DRAIN 2
+
+/* ABI revision of this header; bumped on any signature change. */
+int avo_b200_abi_version(void);
+
+/* Human-readable text for a return code. */
+const char* avo_b200_strerror(int code);
+
+/*
+ * Full attention forward, the drop-in for the candidate's `attention()`
+ * (candidates/cuda_mma_attention/attention_kernel.cu:175-206 `attention_cuda`, and the
+ * guard it enforces, D == 128).  o = softmax(softmax_scale * q k^T [+ causal mask]) v.
+ * causal != 0 masks key j > query i (candidates/cuda_naive_attention/attention_kernel.cu:28).
+ * lse may be null.  seq >= 1 (any length; ragged tails are masked), head_dim == 128,
+ * softmax_scale > 0 (the reference uses 1/sqrt(head_dim), attention_kernel.cu:196).
+ */
+int avo_b200_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int batch,
+                      int heads, int seq, int head_dim, int causal, float softmax_scale,
+                      int* status_dev, void* stream);
+
+/*
+ * Block form used by the context-parallel ring (no reference counterpart: the
+ * reference is single-GPU, avo/benchmark.py:212).  Attention of num_bh heads of
+ * seq_q query rows against seq_kv key/value rows, each head `*_head_stride`
+ * elements apart (rows are 128 elements, contiguous).  The causal mask compares
+ * sequence positions: key row r sits at kv_pos0 + r, query row r at q_pos0 + r.
+ * Writes normalized o (bf16) and lse (fp32, may be null); rows that see no key get
+ * o = 0 and lse = -inf.  Strides must be multiples of 8 elements.
+ */
+int avo_b200_attn_fwd_block(const void* q, const void* k, const void* v, void* o, float* lse,
+                            int num_bh, int seq_q, int seq_kv, int head_dim,
+                            long long q_head_stride, long long kv_head_stride,
+                            long long o_head_stride, long long lse_head_stride, int causal,
+                            float softmax_scale, long long q_pos0, long long kv_pos0,
+                            int* status_dev, void* stream);
+
+/*
+ * Merge one partial result into a running fp32 accumulator by log-sum-exp
+ * (ring context parallelism; no reference counterpart).  For each of num_bh heads
+ * and `rows` rows:  lse' = log(exp(acc_lse) + exp(part_lse)),
+ *                   acc_o' = acc_o * exp(acc_lse - lse') + part_o * exp(part_lse - lse').
+ * acc_o fp32 [num_bh, rows, 128] contiguous, acc_lse fp32 [num_bh, rows];
+ * part_o bf16 with head stride part_o_head_stride (rows contiguous, 128 elements),
+ * part_lse fp32 with head stride part_lse_head_stride.  An accumulator row with
+ * acc_lse = -inf takes the partial as is.
+ */
+int avo_b200_lse_merge(float* acc_o, float* acc_lse, const void* part_o, const float* part_lse,
+                       int num_bh, int rows, int head_dim, long long part_o_head_stride,
+                       long long part_lse_head_stride, void* stream);
+
+/*
+ * Convert a merged fp32 accumulator to the bf16 output: out[h, r, :] = acc_o[h, r, :]
+ * with out rows `out_head_stride` elements apart per head.
+ */
+int avo_b200_acc_to_bf16(const float* acc_o, void* out, int num_bh, int rows, int head_dim,
+                         long long out_head_stride, void* stream);
+
+/*
+ * Self-test of the device watchdog without faulting the GPU: one CTA waits on an
+ * mbarrier that nothing ever completes, with the given limit in microseconds; the
+ * wait expires, the kernel sets AVO_B200_STATUS_WATCHDOG in *status_dev and returns.
+ */
+int avo_b200_watchdog_selftest(int timeout_us, int* status_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AVO_B200_ATTN_H_ */

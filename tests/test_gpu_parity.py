@@ -1,0 +1,138 @@
+"""Parity of the sm_100a kernel (through the C ABI) against the CPU oracle.
+
+Every case draws seeded bf16 inputs on the host (oracle.make_inputs), runs the CUDA
+path on cuda:0 and compares with ``oracle.attention_fp64`` on the same bf16 values:
+max-abs <= 2e-2, mean-abs <= 2e-3 on O, max-abs <= 1e-3 on LSE, plus the reference
+scorer's gate torch.allclose(atol=3e-2, rtol=3e-2) (avo/benchmark.py:638-639).
+"""
+
+from __future__ import annotations
+
+import importlib.util
+import sys
+
+import numpy as np
+import pytest
+
+from oracle import attention_oracle as oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(b200, shape, causal, seed=0, k_scale=1.0):
+    import torch
+
+    q, k, v = oracle.make_inputs(shape, seed=seed, k_scale=k_scale)
+    dq, dk, dv = (t.cuda() for t in (q, k, v))
+    out, lse = b200.attention_forward(dq, dk, dv, causal)
+    torch.cuda.synchronize()
+    b200.check_status(dq.device)
+    return (q, k, v), out.float().cpu().numpy(), lse.cpu().numpy()
+
+
+def _check(inputs, out, lse, causal):
+    import torch
+
+    q, k, v = (t.float().numpy() for t in inputs)
+    ref_o, ref_lse = oracle.attention_fp64(q, k, v, causal)
+    assert np.isfinite(out).all()
+    metrics = oracle.error_metrics(out, ref_o, lse, ref_lse)
+    assert metrics["max_abs"] <= oracle.MAX_ABS_TOL, metrics
+    assert metrics["mean_abs"] <= oracle.MEAN_ABS_TOL, metrics
+    assert metrics["lse_max_abs"] <= oracle.LSE_TOL, metrics
+    assert torch.allclose(torch.from_numpy(out), torch.from_numpy(ref_o).float(),
+                          atol=oracle.ALLCLOSE_ATOL, rtol=oracle.ALLCLOSE_RTOL)
+    return metrics
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_config1_b1_h4_s512(b200, causal):
+    inputs, out, lse = _run(b200, (1, 4, 512, 128), causal)
+    _check(inputs, out, lse, causal)
+
+
+@pytest.mark.parametrize(
+    "shape,causal",
+    [
+        ((1, 1, 128, 128), False),
+        ((1, 1, 128, 128), True),
+        ((1, 2, 256, 128), True),
+        ((2, 3, 384, 128), False),
+        ((2, 3, 384, 128), True),
+        ((1, 2, 100, 128), False),
+        ((1, 2, 100, 128), True),
+        ((1, 1, 1, 128), False),
+        ((1, 1, 1, 128), True),
+        ((1, 2, 1000, 128), True),
+        ((3, 1, 777, 128), False),
+    ],
+)
+def test_ragged_and_small_shapes(b200, shape, causal):
+    inputs, out, lse = _run(b200, shape, causal, seed=3)
+    _check(inputs, out, lse, causal)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_k_scaled_x3_stresses_rescale(b200, causal):
+    inputs, out, lse = _run(b200, (1, 2, 2048, 128), causal, seed=7, k_scale=3.0)
+    _check(inputs, out, lse, causal)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_s4096_two_heads(b200, causal):
+    inputs, out, lse = _run(b200, (1, 2, 4096, 128), causal, seed=11)
+    _check(inputs, out, lse, causal)
+
+
+def test_watchdog_expires_without_fault(b200):
+    import torch
+
+    status = b200.watchdog_selftest("cuda:0", timeout_us=20000)
+    assert status & b200.STATUS_WATCHDOG
+    # The context is still usable afterwards.
+    x = torch.ones(4, device="cuda:0")
+    assert float(x.sum().item()) == 4.0
+
+
+def _load_seed():
+    from pathlib import Path
+
+    path = (Path(__file__).resolve().parents[1] / "avo-ampere_b200" / "candidates"
+            / "cuda_b200_attention_seed.py")
+    spec = importlib.util.spec_from_file_location("avo_candidate_b200_seed", path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def test_candidate_contract_attention_and_lse(b200):
+    import torch
+
+    seed = _load_seed()
+    q, k, v = oracle.make_inputs((1, 4, 512, 128), seed=5)
+    dq, dk, dv = (t.cuda() for t in (q, k, v))
+    out = seed.attention(dq, dk, dv, False)
+    assert out.shape == dq.shape and out.dtype == torch.bfloat16 and out.device == dq.device
+    out2, lse = seed.attention_with_lse(dq, dk, dv, True)
+    assert lse.shape == (1, 4, 512) and lse.dtype == torch.float32
+    torch.cuda.synchronize()
+    _check((q, k, v), out.float().cpu().numpy(),
+           oracle.attention_fp64(*(t.float().numpy() for t in (q, k, v)), False)[1], False)
+    _check((q, k, v), out2.float().cpu().numpy(), lse.cpu().numpy(), True)
+
+
+def test_reference_binding_errors(b200):
+    import torch
+
+    q = torch.zeros((1, 1, 128, 128), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(RuntimeError, match="q must be a CUDA tensor"):
+        b200.attention_forward(q.cpu(), q, q, False)
+    with pytest.raises(RuntimeError, match="contiguous"):
+        b200.attention_forward(q.transpose(2, 3), q, q, False)
+    with pytest.raises(RuntimeError, match="same shape"):
+        b200.attention_forward(q, q[:, :, :64], q, False)
+    with pytest.raises(RuntimeError, match="bf16"):
+        b200.attention_forward(q.half(), q.half(), q.half(), False)
+    with pytest.raises(RuntimeError, match="head_dim must be 128"):
+        z = torch.zeros((1, 1, 128, 64), dtype=torch.bfloat16, device="cuda")
+        b200.attention_forward(z, z, z, False)
