@@ -1,0 +1,492 @@
+"""Throughput benchmark of the B200 attention-forward candidate.
+
+``python bench.py --gpus N --steps K --warmup W [--impl reference]``
+
+One step = one forward of the per-GPU workload (default: B4 H16 S4096 D128
+non-causal, bf16, scale 1/sqrt(128)) through the C-ABI kernel, inputs resident in HBM.
+Under torchrun every rank processes its own head shard of a batch-4N problem (weak
+scaling, no data-path collective); the timed region is bracketed by a barrier and
+``torch.cuda.synchronize()``, timed with CUDA events on the launching stream, and the
+max over ranks is reported.  FLOPs follow the reference accounting
+(avo/benchmark.py:22-27, 54-62): 4*B*H*S^2*D, halved when causal.
+
+``--impl reference`` times the reference's own path for this operation on the host
+cores instead: the seed ``candidates/torch_sdpa_seed.py:6-7`` is
+``F.scaled_dot_product_attention`` (torch 2.11), run here on CPU bf16 tensors (the
+reference scorer itself refuses anything but an sm_86 GPU, avo/benchmark.py:207-215).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "avo-ampere_b200"
+for _p in (str(ROOT), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "attention fwd TFLOPS/GPU (BF16, D=128) at S=4k–32k; % of B200 BF16 peak; 1/2/4/8 GPU"
+UNIT = "TFLOPS"
+FALLBACK_PEAK_TFLOPS = 1590.0
+L2_BYTES = 126 * 1000 * 1000
+
+
+def _load_module(name: str, path: Path):
+    import importlib.util
+
+    module = sys.modules.get(name)
+    if module is None:
+        spec = importlib.util.spec_from_file_location(name, path)
+        module = importlib.util.module_from_spec(spec)
+        sys.modules[name] = module
+        spec.loader.exec_module(module)
+    return module
+
+
+def binding():
+    return _load_module("avo_b200_attention_binding",
+                        PKG / "candidates" / "cuda_b200_attention" / "b200_attention.py")
+
+
+def candidate_seed():
+    return _load_module("avo_candidate_cuda_b200_attention_seed",
+                        PKG / "candidates" / "cuda_b200_attention_seed.py")
+
+
+def measured_peaks() -> tuple[float, float | None, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["bf16_tflops"]), float(data.get("bf16_tflops_sustained") or 0) or None, "measured"
+    except Exception:
+        return FALLBACK_PEAK_TFLOPS, None, "fallback"
+
+
+def profiled_traffic(workload: str) -> float | None:
+    """Per-launch DRAM bytes from the committed ncu summary of this workload, if any."""
+    path = ROOT / "profiles" / f"attn_fwd_{workload}.ncu.txt"
+    if not path.is_file():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+_REASONS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    """Polls SM clock, power and clock-event reasons through NVML on a thread while
+    the timed region runs (reads only; changes no GPU setting)."""
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.period_s = period_s
+        self.samples: list[tuple[int, int, float]] = []
+        self.max_mhz: int | None = None
+        self._stop = threading.Event()
+        self._thread: threading.Thread | None = None
+        self._handle = None
+        self._nvml = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(device_index)
+            handle = None
+            bus = getattr(props, "pci_bus_id", None)
+            if bus is not None:
+                domain = getattr(props, "pci_domain_id", 0)
+                dev = getattr(props, "pci_device_id", 0)
+                try:
+                    handle = pynvml.nvmlDeviceGetHandleByPciBusId(f"{domain:08X}:{bus:02X}:{dev:02X}.0")
+                except Exception:
+                    handle = None
+            if handle is None:
+                handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self._handle, self._nvml = handle, pynvml
+            self.max_mhz = int(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self._handle = None
+
+    def _reasons(self) -> int:
+        nv = self._nvml
+        getter = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or getattr(
+            nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        return int(getter(self._handle))
+
+    def _run(self) -> None:
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = int(nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM))
+                watts = nv.nvmlDeviceGetPowerUsage(self._handle) / 1000.0
+                self.samples.append((mhz, self._reasons(), watts))
+            except Exception:
+                pass
+            time.sleep(self.period_s)
+
+    def __enter__(self):
+        if self._handle is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2.0)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        reasons = 0
+        for _, r, _ in self.samples:
+            reasons |= r
+        names = [name for bit, name in _REASONS.items() if reasons & bit and name != "gpu_idle"]
+        return {
+            "sm_mhz": statistics.median(s[0] for s in self.samples),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": names,
+            "samples": len(self.samples),
+            "power_w_max": max(s[2] for s in self.samples),
+        }
+
+
+# ------------------------------------------------------------------ distributed
+def dist_env() -> tuple[int, int, int]:
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def init_dist(world: int):
+    if world <= 1:
+        return None
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    return dist
+
+
+def max_over_ranks(dist, value: float, device) -> float:
+    if dist is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier_sync(dist, device) -> None:
+    import torch
+
+    if dist is not None:
+        dist.barrier(device_ids=[device.index])
+    torch.cuda.synchronize(device)
+
+
+# ------------------------------------------------------------------ workloads
+def workload_case(name: str):
+    from avo.config import NAMED_CASES
+
+    if name not in NAMED_CASES:
+        raise SystemExit(f"unknown workload {name!r}; choose from {sorted(NAMED_CASES)}")
+    return NAMED_CASES[name]
+
+
+def cpu_sdpa_tflops(case, *, min_seconds: float, max_reps: int, heads: int | None = None):
+    """Time the reference seed's call (torch SDPA) on CPU bf16 tensors, one batch
+    entry of the case (``heads`` heads), all host threads.  Returns (tflops, ms, sample)."""
+    import torch
+
+    from avo.benchmark import attention_forward_flops
+    from avo.config import AttentionCase
+    from oracle.attention_oracle import make_inputs, sdpa_reference
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    h = heads or case.num_heads
+    sample = AttentionCase(seq_len=case.seq_len, causal=case.causal, num_heads=h,
+                           total_tokens=case.seq_len, k_scale=case.k_scale)
+    q, k, v = make_inputs(sample.shape, seed=0, k_scale=sample.k_scale)
+    sdpa_reference(q, k, v, sample.causal)  # warm-up
+    times = []
+    start = time.perf_counter()
+    while len(times) < max_reps and (time.perf_counter() - start < min_seconds or len(times) < 1):
+        t0 = time.perf_counter()
+        sdpa_reference(q, k, v, sample.causal)
+        times.append((time.perf_counter() - t0) * 1000.0)
+    ms = statistics.median(times)
+    flops = attention_forward_flops(sample)
+    desc = (f"torch {torch.__version__} F.scaled_dot_product_attention on CPU bf16, "
+            f"B1 H{h} S{case.seq_len} D128 {'causal' if case.causal else 'non-causal'} "
+            f"(one batch entry of the workload), median of {len(times)} after 1 warm-up")
+    return flops / (ms / 1000.0) / 1e12, ms, desc, torch.get_num_threads()
+
+
+def config_dict(case, n_gpus: int, workload: str) -> dict:
+    per_step_bytes = 4 * case.batch_size * case.num_heads * case.seq_len * case.head_dim * 2
+    return {
+        "workload": f"{workload}: attention forward B{case.batch_size} H{case.num_heads} "
+                    f"S{case.seq_len} D{case.head_dim} {'causal' if case.causal else 'non-causal'} per GPU",
+        "batch_per_gpu": case.batch_size,
+        "global_batch": case.batch_size * n_gpus,
+        "heads": case.num_heads,
+        "seq_len": case.seq_len,
+        "head_dim": case.head_dim,
+        "causal": case.causal,
+        "k_scale": case.k_scale,
+        "parallelism": f"head-sharded x{n_gpus} (no collective)",
+        "l2": f"inputs larger than L2: {per_step_bytes / 1e6:.0f} MB q/k/v/o per step per GPU vs 126 MB L2",
+    }
+
+
+def run_reference(args, case) -> int:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    from avo.benchmark import attention_forward_flops
+    from avo.config import AttentionCase
+    from oracle.attention_oracle import make_inputs, sdpa_reference
+
+    heads = case.num_heads
+    sample = AttentionCase(seq_len=case.seq_len, causal=case.causal, num_heads=heads,
+                           total_tokens=case.seq_len, k_scale=case.k_scale)
+    q, k, v = make_inputs(sample.shape, seed=0, k_scale=sample.k_scale)
+    t0 = time.perf_counter()
+    sdpa_reference(q, k, v, sample.causal)
+    first = time.perf_counter() - t0
+    if first * (args.steps + args.warmup) > 240 and heads > 1:
+        heads = max(1, int(heads * 240 / (first * (args.steps + args.warmup))))
+        sample = AttentionCase(seq_len=case.seq_len, causal=case.causal, num_heads=heads,
+                               total_tokens=case.seq_len, k_scale=case.k_scale)
+        q, k, v = make_inputs(sample.shape, seed=0, k_scale=sample.k_scale)
+    for _ in range(max(0, args.warmup - 1)):
+        sdpa_reference(q, k, v, sample.causal)
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        sdpa_reference(q, k, v, sample.causal)
+        times.append(time.perf_counter() - t)
+    total = sum(times)
+    flops = attention_forward_flops(sample)
+    value = flops * args.steps / total / 1e12
+    desc = (f"torch {torch.__version__} F.scaled_dot_product_attention (the reference seed's call) "
+            f"on CPU bf16, B1 H{heads} S{case.seq_len} D128 per step "
+            f"(one batch entry of the per-GPU workload); time.perf_counter")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total / args.steps * 1000.0, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config_dict(case, args.gpus, args.workload), "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_b200(args, case) -> int:
+    import torch
+
+    from avo.benchmark import attention_forward_flops, host_inputs
+
+    rank, world, local_rank = dist_env()
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = init_dist(world)
+    lib = binding()
+    lib.load_library()
+    seed_mod = candidate_seed()
+
+    # Rank r owns batch entries [4r, 4r+4) of a batch-4N problem: every (b, h) pair
+    # is independent, so each rank draws its own shard with seed + r.
+    q_h, k_h, v_h = host_inputs(case, seed=args.seed + rank)
+    q, k, v = (t.to(device) for t in (q_h, k_h, v_h))
+    out = torch.empty_like(q)
+    flops = attention_forward_flops(case)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        lib.attention_forward(q, k, v, case.causal, need_lse=False, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    lib.check_status(device)
+    barrier_sync(dist, device)
+    sampler = ClockSampler(device.index)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with sampler:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    ms_local = start.elapsed_time(end) / args.steps
+    lib.check_status(device)
+    barrier_sync(dist, device)
+    ms = max_over_ranks(dist, ms_local, device)
+    value = flops * world / (ms / 1000.0) / 1e12
+    per_gpu = flops / (ms_local / 1000.0) / 1e12
+
+    # End to end through the candidate's public attention(): pinned host inputs copied
+    # in, the forward, the output read back, every step.
+    e2e = None
+    if not args.skip_e2e:
+        pq, pk, pv = (t.pin_memory() for t in (q_h, k_h, v_h))
+        po = torch.empty(q_h.shape, dtype=q_h.dtype).pin_memory()
+        dq, dk, dv = (torch.empty_like(q) for _ in range(3))
+
+        def e2e_step():
+            dq.copy_(pq, non_blocking=True)
+            dk.copy_(pk, non_blocking=True)
+            dv.copy_(pv, non_blocking=True)
+            o = seed_mod.attention(dq, dk, dv, case.causal)
+            po.copy_(o, non_blocking=True)
+
+        e2e_steps = max(1, min(args.steps, 20))
+        for _ in range(max(1, min(args.warmup, 3))):
+            e2e_step()
+        barrier_sync(dist, device)
+        s2 = torch.cuda.Event(enable_timing=True)
+        e2 = torch.cuda.Event(enable_timing=True)
+        s2.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e2.record(stream)
+        torch.cuda.synchronize(device)
+        lib.check_status(device)
+        e2e_ms = max_over_ranks(dist, s2.elapsed_time(e2) / e2e_steps, device)
+        nbytes = q_h.numel() * q_h.element_size()
+        e2e = {"value": flops * world / (e2e_ms / 1000.0) / 1e12, "unit": UNIT,
+               "ms_per_step": e2e_ms, "h2d_bytes_per_step": 3 * nbytes,
+               "d2h_bytes_per_step": nbytes,
+               "api": "candidates/cuda_b200_attention_seed.py attention() with pinned host buffers"}
+        del pq, pk, pv, po, dq, dk, dv
+
+    extra = {}
+    if world == 1 and not args.skip_extra:
+        # The throughput target point, same timing rules.
+        from avo.config import NAMED_CASES
+
+        tcase = NAMED_CASES["b4_h16_s8192_noncausal"]
+        tq, tk, tv = (t.to(device) for t in host_inputs(tcase, seed=args.seed))
+        to = torch.empty_like(tq)
+        for _ in range(3):
+            lib.attention_forward(tq, tk, tv, False, need_lse=False, out=to)
+        torch.cuda.synchronize(device)
+        s3 = torch.cuda.Event(enable_timing=True)
+        e3 = torch.cuda.Event(enable_timing=True)
+        reps = max(5, min(args.steps, 30))
+        s3.record(stream)
+        for _ in range(reps):
+            lib.attention_forward(tq, tk, tv, False, need_lse=False, out=to)
+        e3.record(stream)
+        torch.cuda.synchronize(device)
+        lib.check_status(device)
+        t_ms = s3.elapsed_time(e3) / reps
+        t_tflops = attention_forward_flops(tcase) / (t_ms / 1000.0) / 1e12
+        peak, _, _ = measured_peaks()
+        extra["target_point"] = {"workload": "B4 H16 S8192 D128 non-causal", "ms": t_ms,
+                                 "tflops": t_tflops, "frac_of_measured_peak": t_tflops / peak}
+        del tq, tk, tv, to
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.skip_cpu:
+        tflops, cpu_ms, desc, threads = cpu_sdpa_tflops(case, min_seconds=10.0, max_reps=20)
+        cpu = {"value": tflops, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": desc, "ms_per_sample": cpu_ms}
+
+    if rank == 0:
+        peak, sustained, peak_kind = measured_peaks()
+        traffic = profiled_traffic(args.workload)
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": config_dict(case, world, args.workload),
+            "value_per_gpu": value / world,
+            "pct_of_peak": {"measured_burst": value / world / peak,
+                            "measured_sustained": (value / world / sustained) if sustained else None,
+                            "spec_2250": value / world / 2250.0},
+            "roofline": {
+                "bound": "tensor",
+                "achieved": per_gpu,
+                "peak": peak,
+                "unit": "TFLOP/s",
+                "frac": per_gpu / peak,
+                "peak_kind": f"{peak_kind} bf16 burst (MEASURED_PEAKS.json)" if peak_kind == "measured"
+                else "fallback 1.59 PFLOP/s",
+                "flops_per_launch": flops,
+                "traffic": traffic,
+                "algorithmic_bytes_per_launch": 4 * q.numel() * 2,
+            },
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "clocks": sampler.summary(),
+            "cpu_baseline": cpu,
+            **extra,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier(device_ids=[device.index])
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None) -> int:
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=100)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    parser.add_argument("--workload", default="b4_h16_s4096_noncausal")
+    parser.add_argument("--seed", type=int, default=0)
+    parser.add_argument("--skip-e2e", action="store_true")
+    parser.add_argument("--skip-cpu", action="store_true")
+    parser.add_argument("--skip-extra", action="store_true")
+    args = parser.parse_args(argv)
+    if args.warmup < 3 and args.impl == "b200":
+        parser.error("--warmup must be >= 3")
+    case = workload_case(args.workload)
+    if args.impl == "reference":
+        return run_reference(args, case)
+    return run_b200(args, case)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
