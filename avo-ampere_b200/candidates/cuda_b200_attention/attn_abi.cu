@@ -26,12 +26,13 @@ namespace avo_b200 {
 __global__ void lse_merge_kernel(float* __restrict__ acc_o, float* __restrict__ acc_lse,
                                  const __nv_bfloat16* __restrict__ part_o,
                                  const float* __restrict__ part_lse, int num_bh, int rows,
-                                 long long po_hs, long long pl_hs) {
+                                 long long ao_hs, long long al_hs, long long po_hs, long long pl_hs) {
   const long long gw = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= static_cast<long long>(num_bh) * rows) return;
   const long long h = gw / rows, r = gw % rows;
-  const float la = acc_lse[gw];
+  float* lse_slot = acc_lse + h * al_hs + r;
+  const float la = *lse_slot;
   const float lp = part_lse[h * pl_hs + r];
   const float lmax = fmaxf(la, lp);
   float wa = 0.f, wp = 0.f, lnew = -CUDART_INF_F;
@@ -43,7 +44,7 @@ __global__ void lse_merge_kernel(float* __restrict__ acc_o, float* __restrict__ 
     wa /= sum;
     wp /= sum;
   }
-  float4* ap = reinterpret_cast<float4*>(acc_o + gw * kHeadDim) + lane;
+  float4* ap = reinterpret_cast<float4*>(acc_o + h * ao_hs + r * kHeadDim) + lane;
   const uint2 raw = *reinterpret_cast<const uint2*>(part_o + h * po_hs + r * kHeadDim + lane * 4);
   const float2 p01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
   const float2 p23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
@@ -55,16 +56,17 @@ __global__ void lse_merge_kernel(float* __restrict__ acc_o, float* __restrict__ 
                     a.w * wa + p23.y * wp);
   }
   *ap = a;
-  if (lane == 0) acc_lse[gw] = lnew;
+  __syncwarp();
+  if (lane == 0) *lse_slot = lnew;
 }
 
 __global__ void acc_to_bf16_kernel(const float* __restrict__ acc_o, __nv_bfloat16* __restrict__ out,
-                                   int num_bh, int rows, long long out_hs) {
+                                   int num_bh, int rows, long long acc_hs, long long out_hs) {
   const long long gw = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= static_cast<long long>(num_bh) * rows) return;
   const long long h = gw / rows, r = gw % rows;
-  const float4 a = reinterpret_cast<const float4*>(acc_o + gw * kHeadDim)[lane];
+  const float4 a = reinterpret_cast<const float4*>(acc_o + h * acc_hs + r * kHeadDim)[lane];
   uint2 packed;
   packed.x = pack_bf16x2(a.x, a.y);
   packed.y = pack_bf16x2(a.z, a.w);
@@ -266,13 +268,15 @@ extern "C" int avo_b200_attn_fwd_block(const void* q, const void* k, const void*
 }
 
 extern "C" int avo_b200_lse_merge(float* acc_o, float* acc_lse, const void* part_o, const float* part_lse,
-                                  int num_bh, int rows, int head_dim, long long part_o_head_stride,
+                                  int num_bh, int rows, int head_dim, long long acc_o_head_stride,
+                                  long long acc_lse_head_stride, long long part_o_head_stride,
                                   long long part_lse_head_stride, void* stream) {
   if (acc_o == nullptr || acc_lse == nullptr || part_o == nullptr || part_lse == nullptr)
     return AVO_B200_EINVAL;
   if (head_dim != kHeadDim || num_bh < 0 || rows < 0) return AVO_B200_EINVAL;
-  if (part_o_head_stride % 4 != 0 || part_o_head_stride < static_cast<long long>(rows) * kHeadDim ||
-      part_lse_head_stride < rows)
+  const long long row_elems = static_cast<long long>(rows) * kHeadDim;
+  if (acc_o_head_stride % 4 != 0 || part_o_head_stride % 4 != 0 || acc_o_head_stride < row_elems ||
+      part_o_head_stride < row_elems || acc_lse_head_stride < rows || part_lse_head_stride < rows)
     return AVO_B200_EINVAL;
   if (!aligned16(acc_o) || (reinterpret_cast<uintptr_t>(part_o) & 7u) != 0) return AVO_B200_EINVAL;
   const long long warps = static_cast<long long>(num_bh) * rows;
@@ -281,15 +285,17 @@ extern "C" int avo_b200_lse_merge(float* acc_o, float* acc_lse, const void* part
   if (blocks > INT_MAX) return AVO_B200_EINVAL;
   lse_merge_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       acc_o, acc_lse, reinterpret_cast<const __nv_bfloat16*>(part_o), part_lse, num_bh, rows,
-      part_o_head_stride, part_lse_head_stride);
+      acc_o_head_stride, acc_lse_head_stride, part_o_head_stride, part_lse_head_stride);
   return cudaGetLastError() == cudaSuccess ? AVO_B200_OK : AVO_B200_ELAUNCH;
 }
 
 extern "C" int avo_b200_acc_to_bf16(const float* acc_o, void* out, int num_bh, int rows, int head_dim,
-                                    long long out_head_stride, void* stream) {
+                                    long long acc_head_stride, long long out_head_stride, void* stream) {
   if (acc_o == nullptr || out == nullptr || head_dim != kHeadDim || num_bh < 0 || rows < 0)
     return AVO_B200_EINVAL;
-  if (out_head_stride % 4 != 0 || out_head_stride < static_cast<long long>(rows) * kHeadDim)
+  const long long row_elems = static_cast<long long>(rows) * kHeadDim;
+  if (acc_head_stride % 4 != 0 || out_head_stride % 4 != 0 || acc_head_stride < row_elems ||
+      out_head_stride < row_elems)
     return AVO_B200_EINVAL;
   if (!aligned16(acc_o) || (reinterpret_cast<uintptr_t>(out) & 7u) != 0) return AVO_B200_EINVAL;
   const long long warps = static_cast<long long>(num_bh) * rows;
@@ -297,7 +303,7 @@ extern "C" int avo_b200_acc_to_bf16(const float* acc_o, void* out, int num_bh, i
   const long long blocks = (warps * 32 + 255) / 256;
   if (blocks > INT_MAX) return AVO_B200_EINVAL;
   acc_to_bf16_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      acc_o, reinterpret_cast<__nv_bfloat16*>(out), num_bh, rows, out_head_stride);
+      acc_o, reinterpret_cast<__nv_bfloat16*>(out), num_bh, rows, acc_head_stride, out_head_stride);
   return cudaGetLastError() == cudaSuccess ? AVO_B200_OK : AVO_B200_ELAUNCH;
 }
 

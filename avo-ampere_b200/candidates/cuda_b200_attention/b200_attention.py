@@ -40,9 +40,9 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     ),
     "avo_b200_lse_merge": (
         _c_int,
-        [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_ll, _c_ll, _vp],
+        [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_ll, _c_ll, _c_ll, _c_ll, _vp],
     ),
-    "avo_b200_acc_to_bf16": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_ll, _vp]),
+    "avo_b200_acc_to_bf16": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_ll, _c_ll, _vp]),
     "avo_b200_watchdog_selftest": (_c_int, [_c_int, _vp, _vp]),
 }
 ABI_VERSION = 1
@@ -231,36 +231,53 @@ def attention_block(q, k, v, out, lse, *, causal: bool, q_pos0: int, kv_pos0: in
     _check(code, "avo_b200_attn_fwd_block")
 
 
+def _rows_view(t, name, dtype):
+    if t.dim() != 3 or t.shape[2] != HEAD_DIM or t.stride(2) != 1 or t.stride(1) != HEAD_DIM:
+        raise RuntimeError(f"{name} must be [num_bh, rows, 128] with contiguous rows")
+    if t.dtype != dtype:
+        raise RuntimeError(f"{name} must be {dtype}")
+
+
+def _lse_view(t, name):
+    torch = _torch()
+    if t.dim() != 2 or t.stride(1) != 1 or t.dtype != torch.float32:
+        raise RuntimeError(f"{name} must be fp32 [num_bh, rows] with contiguous rows")
+
+
 def lse_merge(acc_o, acc_lse, part_o, part_lse) -> None:
     """Fold one partial (bf16 O, fp32 LSE) into fp32 accumulators by log-sum-exp."""
     torch = _torch()
+    _rows_view(acc_o, "acc_o", torch.float32)
+    _rows_view(part_o, "part_o", torch.bfloat16)
+    _lse_view(acc_lse, "acc_lse")
+    _lse_view(part_lse, "part_lse")
+    if acc_o.shape != part_o.shape or tuple(acc_lse.shape) != tuple(acc_o.shape[:2]) or \
+            tuple(part_lse.shape) != tuple(acc_o.shape[:2]):
+        raise RuntimeError("lse_merge shapes disagree")
     num_bh, rows, head_dim = (int(x) for x in acc_o.shape)
-    if not acc_o.is_contiguous() or acc_o.dtype != torch.float32:
-        raise RuntimeError("acc_o must be contiguous fp32 [num_bh, rows, 128]")
-    if not acc_lse.is_contiguous() or acc_lse.dtype != torch.float32:
-        raise RuntimeError("acc_lse must be contiguous fp32 [num_bh, rows]")
-    if part_o.stride(2) != 1 or part_o.stride(1) != HEAD_DIM or part_o.dtype != torch.bfloat16:
-        raise RuntimeError("part_o must be bf16 [num_bh, rows, 128] with contiguous rows")
     lib = load_library()
     with torch.cuda.device(acc_o.device):
         code = lib.avo_b200_lse_merge(
             acc_o.data_ptr(), acc_lse.data_ptr(), part_o.data_ptr(), part_lse.data_ptr(),
-            num_bh, rows, head_dim, part_o.stride(0), part_lse.stride(0),
-            _stream_handle(acc_o.device),
+            num_bh, rows, head_dim, acc_o.stride(0), acc_lse.stride(0), part_o.stride(0),
+            part_lse.stride(0), _stream_handle(acc_o.device),
         )
     _check(code, "avo_b200_lse_merge")
 
 
 def acc_to_bf16(acc_o, out) -> None:
+    """out (bf16) = acc_o (fp32), both [num_bh, rows, 128] with contiguous rows."""
     torch = _torch()
+    _rows_view(acc_o, "acc_o", torch.float32)
+    _rows_view(out, "out", torch.bfloat16)
+    if acc_o.shape != out.shape:
+        raise RuntimeError("acc_to_bf16 shapes disagree")
     num_bh, rows, head_dim = (int(x) for x in acc_o.shape)
-    if out.stride(2) != 1 or out.stride(1) != HEAD_DIM or out.dtype != torch.bfloat16:
-        raise RuntimeError("out must be bf16 [num_bh, rows, 128] with contiguous rows")
     lib = load_library()
     with torch.cuda.device(acc_o.device):
         code = lib.avo_b200_acc_to_bf16(
-            acc_o.data_ptr(), out.data_ptr(), num_bh, rows, head_dim, out.stride(0),
-            _stream_handle(acc_o.device),
+            acc_o.data_ptr(), out.data_ptr(), num_bh, rows, head_dim, acc_o.stride(0),
+            out.stride(0), _stream_handle(acc_o.device),
         )
     _check(code, "avo_b200_acc_to_bf16")
 

@@ -2,7 +2,7 @@
 
 Obeys the candidate contract of the AVO scorer: a module-level callable
 ``attention(q, k, v, causal) -> Tensor[B, H, S, D]`` (reference: loader
-avo/benchmark.py:406-418, oracle seed candidates/torch_sdpa_seed.py:6-7).  Inputs are
+avo/benchmark.py:406-418; the SDPA seed candidates/torch_sdpa_seed.py:6-7).  Inputs are
 contiguous CUDA bf16 ``[B, H, S, 128]``; the output is a new tensor of the same shape
 and dtype, as ``torch::empty_like`` gives in the reference seeds
 (candidates/cuda_mma_attention/attention_kernel.cu:188).

@@ -84,21 +84,22 @@ int avo_b200_attn_fwd_block(const void* q, const void* k, const void* v, void* o
  * (ring context parallelism; no reference counterpart).  For each of num_bh heads
  * and `rows` rows:  lse' = log(exp(acc_lse) + exp(part_lse)),
  *                   acc_o' = acc_o * exp(acc_lse - lse') + part_o * exp(part_lse - lse').
- * acc_o fp32 [num_bh, rows, 128] contiguous, acc_lse fp32 [num_bh, rows];
- * part_o bf16 with head stride part_o_head_stride (rows contiguous, 128 elements),
- * part_lse fp32 with head stride part_lse_head_stride.  An accumulator row with
- * acc_lse = -inf takes the partial as is.
+ * acc_o fp32 and part_o bf16 are [num_bh, rows, 128] with contiguous 128-element rows
+ * and the given head strides (elements); acc_lse and part_lse are fp32 [num_bh, rows]
+ * with contiguous rows and the given head strides.  An accumulator row with
+ * acc_lse = -inf takes the partial as is (its acc_o contents are ignored).
  */
 int avo_b200_lse_merge(float* acc_o, float* acc_lse, const void* part_o, const float* part_lse,
-                       int num_bh, int rows, int head_dim, long long part_o_head_stride,
+                       int num_bh, int rows, int head_dim, long long acc_o_head_stride,
+                       long long acc_lse_head_stride, long long part_o_head_stride,
                        long long part_lse_head_stride, void* stream);
 
 /*
- * Convert a merged fp32 accumulator to the bf16 output: out[h, r, :] = acc_o[h, r, :]
- * with out rows `out_head_stride` elements apart per head.
+ * Convert a merged fp32 accumulator to the bf16 output: out[h, r, :] = acc_o[h, r, :],
+ * both [num_bh, rows, 128] with contiguous rows and the given head strides (elements).
  */
 int avo_b200_acc_to_bf16(const float* acc_o, void* out, int num_bh, int rows, int head_dim,
-                         long long out_head_stride, void* stream);
+                         long long acc_head_stride, long long out_head_stride, void* stream);
 
 /*
  * Self-test of the device watchdog without faulting the GPU: one CTA waits on an
