@@ -193,7 +193,8 @@ def error_metrics(out, ref_o, lse=None, ref_lse=None) -> dict:
         lse = np.asarray(lse, dtype=np.float64)
         ref_lse = np.asarray(ref_lse, dtype=np.float64)
         both_inf = np.isneginf(lse) & np.isneginf(ref_lse)
-        d = np.where(both_inf, 0.0, np.abs(lse - ref_lse))
+        with np.errstate(invalid="ignore"):
+            d = np.where(both_inf, 0.0, np.abs(lse - ref_lse))
         metrics["lse_max_abs"] = float(d.max()) if d.size else 0.0
     return metrics
 
