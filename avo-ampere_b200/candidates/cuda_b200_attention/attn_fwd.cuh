@@ -32,6 +32,12 @@
 
 #include "sm100_ptx.cuh"
 
+// Optional per-tile timeline hooks (role, tile, event) for development builds; they
+// compile to nothing unless a build defines AVO_TRACE_HOOK before including this file.
+#ifndef AVO_TRACE_HOOK
+#define AVO_TRACE_HOOK(role, tile, event)
+#endif
+
 namespace avo_b200 {
 
 constexpr int kHeadDim = 128;
@@ -40,13 +46,29 @@ constexpr int kQTiles = 2;                     // Q tiles per CTA
 constexpr int kRowsPerCta = kBlockM * kQTiles; // 256
 constexpr int kBlockN = 128;                   // keys per K/V tile
 constexpr int kStages = 4;                     // K/V ring depth
+// K/V tiles are also prefetched into L2 this many ring positions ahead of their
+// shared-memory load: the CTAs that share a head reach each tile together, so
+// without it every tile's first touch pays full HBM latency inside the ring.
+constexpr int kPrefetchAhead = 8;
 constexpr int kTileBytes = 128 * kHeadDim * 2; // 32 KiB: 128 rows x 128 bf16
 constexpr int kHalfBytes = kTileBytes / 2;     // one 64-column, 128B-swizzled half
 constexpr int kLoadWarp = 8;
 constexpr int kMmaWarp = 9;
-constexpr int kThreads = 320;
+constexpr int kWaitWarp = 10;
+// Named barriers: 0 = __syncthreads, 1/2 = epilogue of softmax warpgroup 0/1,
+// 3 = waiter -> MMA warp release (64 threads).
+constexpr uint32_t kBarMmaHandoff = 3;
+constexpr int kThreads = 384;                  // 3 warpgroups: softmax 0, softmax 1, load/MMA
+// Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512), the
+// load/MMA warpgroup drops to 88 and each softmax warpgroup rises to 208:
+// 2 x 128 x 208 + 128 x 88 = 64512 (no spills in either role).
+constexpr uint32_t kRegsLaunch = 168;
+constexpr uint32_t kRegsSoftmax = 208;
+constexpr uint32_t kRegsOther = 88;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunch, "register split");
 constexpr uint32_t kTmemCols = 512;            // S0 | S1 | O0 | O1, 128 columns each
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: rescale only past 2^8 growth
+constexpr int kEmuPairsPer8 = 2;               // FMA-pipe exp2 share: 2 of every 8 pairs
 
 // Device status bits (OR-ed into the caller's status word).
 constexpr int kStatusWatchdog = 1;  // a pipeline wait exceeded the watchdog; outputs invalid
@@ -61,8 +83,8 @@ enum : int {
   BAR_KV_FULL = 1,
   BAR_KV_EMPTY = BAR_KV_FULL + kStages,
   BAR_S_FULL = BAR_KV_EMPTY + kStages,
-  BAR_P_READY = BAR_S_FULL + kQTiles,
-  BAR_O_DONE = BAR_P_READY + kQTiles,
+  BAR_P_HALF = BAR_S_FULL + kQTiles,  // [2*tile + half]: P half published (one arrive per warp)
+  BAR_O_DONE = BAR_P_HALF + 2 * kQTiles,
   BAR_DRAIN = BAR_O_DONE + kQTiles,
   NUM_BARS = BAR_DRAIN + 1
 };
@@ -133,14 +155,16 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_smem, uint3
   }
 }
 
-// O += P V: P (128 x 128 keys, bf16) from TMEM, V (128 keys x 128 dims) from shared
-// memory as an MN-major operand: dims contiguous, the two 64-dim halves 16 KiB apart
-// (leading byte offset), 8-key groups 1024 B apart (stride byte offset).
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_smem,
-                                         uint32_t accumulate) {
+// O += P V over keys [64*half, 64*half + 64): P (128 rows x keys, bf16) from TMEM,
+// V (keys x 128 dims) from shared memory as an MN-major operand: dims contiguous, the
+// two 64-dim halves 16 KiB apart (leading byte offset), 8-key groups 1024 B apart
+// (stride byte offset).
+__device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_smem, int half,
+                                              uint32_t accumulate) {
   constexpr uint32_t idesc = idesc_bf16_f32(kBlockM, kHeadDim, 0, 1);
 #pragma unroll
-  for (int kk = 0; kk < kBlockN / 16; ++kk) {
+  for (int q = 0; q < 4; ++q) {
+    const int kk = half * 4 + q;
     mma_ts(d_tmem, p_tmem + kk * 8, smem_desc_sw128(v_smem + kk * 16 * 128, kHalfBytes, 1024), idesc,
            (accumulate | (kk > 0 ? 1u : 0u)));
   }
@@ -148,6 +172,35 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
 
 __device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
 __device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
+
+// P for 64 keys (two 32-column chunks of S): x = s*scale - m by packed FMA, p = 2^x,
+// row sums accumulated in packed pairs, P packed to bf16x2 for tcgen05.st.  kMix
+// routes kEmuPairsPer8 of every 8 pairs through the FMA-pipe exp2; the choice is a
+// template parameter so each variant is straight-line code the compiler can
+// interleave (MUFU and FMA chains side by side).
+template <bool kMix>
+__device__ __forceinline__ void exp_half(const uint32_t (&sa)[32], const uint32_t (&sb)[32],
+                                         uint64_t scale2, uint64_t neg_m2, uint64_t (&sum2)[2],
+                                         uint32_t (&pk)[32]) {
+#pragma unroll
+  for (int cc = 0; cc < 2; ++cc) {
+    const uint32_t (&sc)[32] = cc == 0 ? sa : sb;
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+      const uint64_t x2 = f2_fma(f2_pack(u2f(sc[e]), u2f(sc[e + 1])), scale2, neg_m2);
+      float x0, x1, p0, p1;
+      f2_unpack(x2, x0, x1);
+      if (kMix && ((e >> 1) & 7) < kEmuPairsPer8) {
+        exp2_poly_x2(f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f)), p0, p1);
+      } else {
+        p0 = ex2_approx(x0);
+        p1 = ex2_approx(x1);
+      }
+      sum2[(e >> 1) & 1] = f2_add(sum2[(e >> 1) & 1], f2_pack(p0, p1));
+      pk[cc * 16 + (e >> 1)] = pack_bf16x2(p0, p1);
+    }
+  }
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -191,7 +244,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < kQTiles; ++i) {
       mbar_init(bar(BAR_S_FULL + i), 1);
-      mbar_init(bar(BAR_P_READY + i), kBlockM);
+      mbar_init(bar(BAR_P_HALF + 2 * i + 0), kBlockM / 32);
+      mbar_init(bar(BAR_P_HALF + 2 * i + 1), kBlockM / 32);
       mbar_init(bar(BAR_O_DONE + i), 1);
     }
     mbar_init(bar(BAR_DRAIN), 1);
@@ -217,6 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sRing = sbase + kSmemRing;
 
   if (warp < 2 * 4) {
+    regs_increase<kRegsSoftmax>();
     // ------------------------------------------------------------ softmax warpgroups
     const int i = warp >> 2;          // Q tile of this warpgroup
     const int wq = warp & 3;          // TMEM lane quarter of this warp
@@ -236,12 +291,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < n_tiles; ++j) {
       ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_S_FULL + i), j & 1, watch));
       if (!ok) break;
+      AVO_TRACE_HOOK(i, j, 0);
       tc_fence_after();
       uint32_t s[4][32];
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_wait_ld(s[c]);
+      AVO_TRACE_HOOK(i, j, 1);
 
       const int key_base = j * kBlockN;
       const bool tail = key_base + kBlockN > p.seq_kv;
@@ -256,60 +313,96 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (c * 32 + e >= lim) s[c][e] = f2u(-CUDART_INF_F);
       }
 
+      // Speculative P for keys 0-63 against the running max, computed side by side
+      // with the row max over all 128 scores (independent instruction streams).  The
+      // running max only moves when the tile max exceeds it by more than 2^8, so the
+      // speculation almost always stands; when it does not (first tile, rare jumps)
+      // the half is recomputed with the new max, giving exactly the values a
+      // max-first order would.  An overflow of the speculative exp2 implies a move.
+      const bool mix = !(tail || diag);
+      const uint64_t scale2 = f2_pack(scale, scale);
+      uint64_t neg_m2 = f2_pack((m == -CUDART_INF_F) ? 0.f : -m, (m == -CUDART_INF_F) ? 0.f : -m);
+      uint64_t sum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+      uint32_t pk[32];
+      if (mix) {
+        exp_half<true>(s[0], s[1], scale2, neg_m2, sum2, pk);
+      } else {
+        exp_half<false>(s[0], s[1], scale2, neg_m2, sum2, pk);
+      }
       float mx[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mx[e] = -CUDART_INF_F;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int e = 0; e < 32; ++e) mx[e & 7] = fmaxf(mx[e & 7], u2f(s[c][e]));
-      float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                       fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        for (int e = 0; e < 32; e += 2)
+          mx[((c * 32 + e) >> 1) & 7] = fmax3(mx[((c * 32 + e) >> 1) & 7], u2f(s[c][e]), u2f(s[c][e + 1]));
+      const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
       const float m_new = fmaxf(m, mt * scale);
       const bool grow = m_new > m + kRescaleThreshold;
-      float factor = 1.f;
-      if (grow) {
-        factor = ex2_approx(m - m_new);
-        l *= factor;
-        m = m_new;
-      }
-      const float neg_m = (m == -CUDART_INF_F) ? 0.f : -m;
+      AVO_TRACE_HOOK(i, j, 2);
 
-      uint32_t pk[2][32];
-      float rs[4] = {0.f, 0.f, 0.f, 0.f};
+      if (__any_sync(0xffffffffu, grow)) {
+        float factor = 1.f;
+        if (grow) {
+          factor = ex2_approx(m - m_new);
+          l *= factor;
+          m = m_new;
+        }
+        const float neg_m = (m == -CUDART_INF_F) ? 0.f : -m;
+        neg_m2 = f2_pack(neg_m, neg_m);
+        sum2[0] = f2_pack(0.f, 0.f);
+        sum2[1] = f2_pack(0.f, 0.f);
+        if (mix) {
+          exp_half<true>(s[0], s[1], scale2, neg_m2, sum2, pk);
+        } else {
+          exp_half<false>(s[0], s[1], scale2, neg_m2, sum2, pk);
+        }
+        if (j > 0) {
+          // O holds P V summed over tiles < j relative to the old max.  The last of
+          // those MMAs completed before S_j did (same issuing thread, in order);
+          // rescale this row in TMEM before any part of P_j is published.
+          ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (j - 1) & 1, watch));
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld(o);
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float p0 = ex2_approx(fmaf(u2f(s[c][e]), scale, neg_m));
-          const float p1 = ex2_approx(fmaf(u2f(s[c][e + 1]), scale, neg_m));
-          rs[(e >> 1) & 3] += p0 + p1;
-          pk[c >> 1][(c & 1) * 16 + (e >> 1)] = pack_bf16x2(p0, p1);
+            for (int e = 0; e < 32; ++e) o[e] = f2u(u2f(o[e]) * factor);
+            tmem_st32(tO + c * 32, o);
+          }
         }
       }
-      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
-      tmem_st32(tS + 0, pk[0]);
-      tmem_st32(tS + 32, pk[1]);
 
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // O holds P V summed over tiles < j relative to the old max: wait for the
-        // last of those MMAs, then rescale this row in TMEM.
-        ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (j - 1) & 1, watch));
-        if (!ok) break;
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
-          tmem_wait_ld(o);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = f2u(u2f(o[e]) * factor);
-          tmem_st32(tO + c * 32, o);
-        }
-      }
+      // Publish P in two 64-key halves, each as soon as it sits in TMEM, so PV on keys
+      // 0-63 overlaps the exps of keys 64-127.  On unmasked tiles kEmuPairsPer8 of
+      // every 8 pairs take the FMA-pipe exp2 (exp2_poly_x2) to offload the MUFU
+      // unit; masked tiles use ex2.approx only, which returns exactly 0 for masked
+      // (-inf) scores.
+      tmem_st32(tS, pk);
       tc_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(BAR_P_READY + i));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(BAR_P_HALF + 2 * i + 0));
+      if (mix) {
+        exp_half<true>(s[2], s[3], scale2, neg_m2, sum2, pk);
+      } else {
+        exp_half<false>(s[2], s[3], scale2, neg_m2, sum2, pk);
+      }
+      AVO_TRACE_HOOK(i, j, 3);
+      tmem_st32(tS + 32, pk);
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(BAR_P_HALF + 2 * i + 1));
+      float a0, a1, b0, b1;
+      f2_unpack(sum2[0], a0, a1);
+      f2_unpack(sum2[1], b0, b1);
+      l += (a0 + a1) + (b0 + b1);
+      AVO_TRACE_HOOK(i, j, 4);
     }
 
     if (ok && n_tiles > 0) {
@@ -356,6 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bulk_wait_group_read0();
     }
   } else if (warp == kLoadWarp) {
+    regs_decrease<kRegsOther>();
     // ------------------------------------------------------------ TMA producer
     if (lane == 0 && n_tiles > 0) {
       const uint64_t pol_q = policy_evict_first();
@@ -366,10 +460,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(sQ + i * kTileBytes + h * kHalfBytes, &tm_q, bar(BAR_Q), h * 64, q0 + i * kBlockM, bh,
                       pol_q);
       int issued = 0;
-      for (int tt = 0; tt < 2 * n_tiles; ++tt) {
+      const int n_loads = 2 * n_tiles;
+      for (int tt = 0; tt < min(kPrefetchAhead, n_loads); ++tt) {
+        const CUtensorMap* tm = (tt & 1) ? &tm_v : &tm_k;
+        tma_prefetch_3d(tm, 0, (tt >> 1) * kBlockN, bh);
+        tma_prefetch_3d(tm, 64, (tt >> 1) * kBlockN, bh);
+      }
+      for (int tt = 0; tt < n_loads; ++tt) {
         const int slot = tt % kStages;
         const int use = tt / kStages;
         if (use > 0 && !wait_phase(bar(BAR_KV_EMPTY + slot), (use - 1) & 1, watch)) break;
+        AVO_TRACE_HOOK(3, tt >> 1, tt & 1);
         mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), kTileBytes);
         const CUtensorMap* tm = (tt & 1) ? &tm_v : &tm_k;
         const int krow = (tt >> 1) * kBlockN;
@@ -377,6 +478,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(sRing + slot * kTileBytes + h * kHalfBytes, tm, bar(BAR_KV_FULL + slot), h * 64, krow,
                       bh, pol_kv);
         issued = tt + 1;
+        if (tt + kPrefetchAhead < n_loads) {
+          const int pt = tt + kPrefetchAhead;
+          const CUtensorMap* ptm = (pt & 1) ? &tm_v : &tm_k;
+          tma_prefetch_3d(ptm, 0, (pt >> 1) * kBlockN, bh);
+          tma_prefetch_3d(ptm, 64, (pt >> 1) * kBlockN, bh);
+        }
       }
       if (*abort_flag) {
         // Copies already issued still land in shared memory: wait for them.  Slot s
@@ -388,53 +495,120 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
+    regs_decrease<kRegsOther>();
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && n_tiles > 0) {
+    // The whole warp runs the schedule and lane 0 issues.  It never reads shared
+    // memory between MMA groups: on sm_100 any such read (an mbarrier wait included)
+    // completes only after this thread's queued tcgen05.mma instructions have
+    // drained, leaving the tensor pipe idle while it refills.  Instead the waiter
+    // warp performs every mbarrier wait and releases this warp through a hardware
+    // named barrier, which does not drain the queue.  Both warps take the same
+    // number of rounds (a function of n_tiles only), including after a watchdog
+    // abort, so neither can be left waiting.
+    if (n_tiles > 0) {
+      const bool leader = lane == 0;
       const uint32_t tS0 = tmem, tS1 = tmem + kBlockN;
       const uint32_t tO0 = tmem + 2 * kBlockN, tO1 = tO0 + kHeadDim;
       const uint32_t sQ0 = sQ, sQ1 = sQ + kTileBytes;
-      bool ok = wait_phase(bar(BAR_Q), 0, watch) && wait_phase(bar(BAR_KV_FULL + 0), 0, watch);
-      if (ok) {
+      auto released = [&]() {
+        __syncwarp();
+        named_bar_sync(kBarMmaHandoff, 64);
         tc_fence_after();
+      };
+      released();  // Q and K_0 resident
+      if (leader) {
         issue_qk(tS0, sQ0, sRing);
         mma_commit(bar(BAR_S_FULL + 0));
         issue_qk(tS1, sQ1, sRing);
         mma_commit(bar(BAR_S_FULL + 1));
         mma_commit(bar(BAR_KV_EMPTY + 0));
       }
-      for (int j = 0; ok && j < n_tiles; ++j) {
+      for (int j = 0; j < n_tiles; ++j) {
         const int tv = 2 * j + 1, sv = tv % kStages;
         const int tk = 2 * j + 2, sk = tk % kStages;
         const bool more = j + 1 < n_tiles;
         const uint32_t v_smem = sRing + sv * kTileBytes;
         const uint32_t k_smem = sRing + sk * kTileBytes;
-        if (!wait_phase(bar(BAR_KV_FULL + sv), (tv / kStages) & 1, watch)) break;
-        if (!wait_phase(bar(BAR_P_READY + 0), j & 1, watch)) break;
-        tc_fence_after();
-        issue_pv(tO0, tS0, v_smem, j > 0 ? 1u : 0u);
-        mma_commit(bar(BAR_O_DONE + 0));
-        if (more) {
-          if (!wait_phase(bar(BAR_KV_FULL + sk), (tk / kStages) & 1, watch)) break;
-          tc_fence_after();
-          issue_qk(tS0, sQ0, k_smem);
-          mma_commit(bar(BAR_S_FULL + 0));
+        released();  // V_j resident, keys 0-63 of P0_j published
+        AVO_TRACE_HOOK(2, j, 0);
+        if (leader) issue_pv_half(tO0, tS0, v_smem, 0, j > 0 ? 1u : 0u);
+        released();  // keys 64-127 of P0_j published
+        if (leader) {
+          issue_pv_half(tO0, tS0, v_smem, 1, 1u);
+          mma_commit(bar(BAR_O_DONE + 0));
         }
-        if (!wait_phase(bar(BAR_P_READY + 1), j & 1, watch)) break;
-        tc_fence_after();
-        issue_pv(tO1, tS1, v_smem, j > 0 ? 1u : 0u);
-        mma_commit(bar(BAR_O_DONE + 1));
-        mma_commit(bar(BAR_KV_EMPTY + sv));
+        AVO_TRACE_HOOK(2, j, 1);
         if (more) {
-          issue_qk(tS1, sQ1, k_smem);
-          mma_commit(bar(BAR_S_FULL + 1));
-          mma_commit(bar(BAR_KV_EMPTY + sk));
+          released();  // K_{j+1} resident
+          if (leader) {
+            issue_qk(tS0, sQ0, k_smem);
+            mma_commit(bar(BAR_S_FULL + 0));
+          }
         }
+        AVO_TRACE_HOOK(2, j, 2);
+        released();  // keys 0-63 of P1_j published
+        AVO_TRACE_HOOK(2, j, 3);
+        if (leader) issue_pv_half(tO1, tS1, v_smem, 0, j > 0 ? 1u : 0u);
+        released();  // keys 64-127 of P1_j published
+        if (leader) {
+          issue_pv_half(tO1, tS1, v_smem, 1, 1u);
+          mma_commit(bar(BAR_O_DONE + 1));
+          mma_commit(bar(BAR_KV_EMPTY + sv));
+          if (more) {
+            issue_qk(tS1, sQ1, k_smem);
+            mma_commit(bar(BAR_S_FULL + 1));
+            mma_commit(bar(BAR_KV_EMPTY + sk));
+          }
+        }
+        AVO_TRACE_HOOK(2, j, 4);
       }
-      // Every MMA issued above completes before TMEM and shared memory are released.
-      mma_commit(bar(BAR_DRAIN));
-      drain_phase(bar(BAR_DRAIN), 0, watch);
+      __syncwarp();
+      if (leader) {
+        // Every MMA issued above completes before TMEM and shared memory are released.
+        mma_commit(bar(BAR_DRAIN));
+        drain_phase(bar(BAR_DRAIN), 0, watch);
+      }
     }
     __syncwarp();
+  } else if (warp == kWaitWarp) {
+    regs_decrease<kRegsOther>();
+    // ------------------------------------------------------------ waiter
+    // Performs, in the MMA warp's consumption order, every mbarrier wait that gates
+    // an MMA group, then releases the MMA warp (see above).  After an abort its
+    // waits return at once and it only keeps the round count.
+    if (n_tiles > 0) {
+      auto release = [&]() {
+        __syncwarp();
+        named_bar_sync(kBarMmaHandoff, 64);
+      };
+      if (lane == 0) {
+        wait_phase(bar(BAR_Q), 0, watch);
+        wait_phase(bar(BAR_KV_FULL + 0), 0, watch);
+      }
+      release();
+      for (int j = 0; j < n_tiles; ++j) {
+        const int tv = 2 * j + 1, sv = tv % kStages;
+        const int tk = 2 * j + 2, sk = tk % kStages;
+        if (lane == 0) {
+          wait_phase(bar(BAR_KV_FULL + sv), (tv / kStages) & 1, watch);
+          wait_phase(bar(BAR_P_HALF + 0), j & 1, watch);
+        }
+        release();
+        if (lane == 0) wait_phase(bar(BAR_P_HALF + 1), j & 1, watch);
+        release();
+        if (j + 1 < n_tiles) {
+          if (lane == 0) wait_phase(bar(BAR_KV_FULL + sk), (tk / kStages) & 1, watch);
+          release();
+        }
+        if (lane == 0) wait_phase(bar(BAR_P_HALF + 2), j & 1, watch);
+        release();
+        if (lane == 0) wait_phase(bar(BAR_P_HALF + 3), j & 1, watch);
+        release();
+      }
+    }
+    __syncwarp();
+  } else {
+    regs_decrease<kRegsOther>();  // warp 11 completes the load/MMA/waiter warpgroup
   }
 
   tc_fence_before();

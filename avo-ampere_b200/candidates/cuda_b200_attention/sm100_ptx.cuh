@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the attention kernel uses:
-// mbarriers, TMA tensor copies (no cluster multicast anywhere), tcgen05 MMA /
+// mbarriers, TMA tensor copies (plain per-CTA tiles only), tcgen05 MMA /
 // TMEM load-store / commit / fences, and the UMMA shared-memory and instruction
 // descriptors.  Every wrapper maps to one documented PTX instruction.
 #pragma once
@@ -57,7 +57,7 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
 }
 
 // 3-D tiled bulk-tensor load global -> shared, completion counted on `bar` in bytes.
-// The destination is this CTA's own shared memory; no multicast form is used.
+// The destination is this CTA's own shared memory only.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int c0, int c1, int c2, uint64_t cache_policy) {
   asm volatile(
@@ -65,6 +65,14 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "l"(cache_policy)
       : "memory");
+}
+
+// Prefetch one 3-D box of a tensor into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
 }
 
 // 3-D tiled bulk-tensor store shared -> global (bulk-group completion).
@@ -101,6 +109,18 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
   return p;
+}
+
+// ---------------------------------------------------------------- register reallocation
+// Per-warpgroup register budget changes; every warp of the warpgroup executes the same one.
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_increase() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_decrease() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
 }
 
 // ---------------------------------------------------------------- named barriers
@@ -238,6 +258,62 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Three-input maximum (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed pairs of fp32 in one 64-bit register (sm_100 f32x2 arithmetic).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x on the FMA pipe for a pair of inputs x in [-125, 127] (callers clamp below):
+// Cody-Waite split x = j + f with j = round(x), taken from the low mantissa bits of
+// x + 1.5*2^23, and f in [-1/2, 1/2]; 2^f by a degree-3 relative-minimax polynomial
+// (coefficients from exp2_poly.py, relative error < 7.5e-5); 2^j applied by adding
+// j << 23 to the polynomial's bit pattern.
+__device__ __forceinline__ void exp2_poly_x2(uint64_t x2, float& r0, float& r1) {
+  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t neg_magic = f2_pack(-12582912.0f, -12582912.0f);
+  const uint64_t minus_one = f2_pack(-1.0f, -1.0f);
+  const uint64_t c3 = f2_pack(0.0551716685295105f, 0.0551716685295105f);
+  const uint64_t c2 = f2_pack(0.2426111251115799f, 0.2426111251115799f);
+  const uint64_t c1 = f2_pack(0.6932609677314758f, 0.6932609677314758f);
+  const uint64_t c0 = f2_pack(0.9999280571937561f, 0.9999280571937561f);
+  const uint64_t t2 = f2_add(x2, magic);        // 1.5*2^23 + round(x)
+  const uint64_t j2 = f2_add(t2, neg_magic);    // round(x), exact
+  const uint64_t f2 = f2_fma(j2, minus_one, x2);  // x - round(x), exact
+  uint64_t p2 = f2_fma(c3, f2, c2);
+  p2 = f2_fma(p2, f2, c1);
+  p2 = f2_fma(p2, f2, c0);
+  float p0, p1, t0, t1;
+  f2_unpack(p2, p0, p1);
+  f2_unpack(t2, t0, t1);
+  r0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  r1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
 // Packs two floats to bf16x2 with round-to-nearest-even: `lo` in bits 0-15.
