@@ -57,7 +57,7 @@ const char* avo_b200_strerror(int code);
  * guard it enforces, D == 128).  o = softmax(softmax_scale * q k^T [+ causal mask]) v.
  * causal != 0 masks key j > query i (candidates/cuda_naive_attention/attention_kernel.cu:28).
  * lse may be null.  seq >= 1 (any length; ragged tails are masked), head_dim == 128,
- * softmax_scale > 0 (the reference uses 1/sqrt(head_dim), attention_kernel.cu:196).
+ * softmax_scale > 0 (the reference uses 1/sqrt(head_dim), attention_kernel.cu:198).
  */
 int avo_b200_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int batch,
                       int heads, int seq, int head_dim, int causal, float softmax_scale,
