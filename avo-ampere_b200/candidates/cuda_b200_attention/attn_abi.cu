@@ -154,6 +154,15 @@ int prepare_device() {
     (void)cudaGetLastError();
     return AVO_B200_ELAUNCH;
   }
+  // The kernel rebalances registers between warpgroups with setmaxnreg, which only
+  // works out if the launch allocation is exactly the one the split was computed for;
+  // otherwise an increase could wait forever.  Refuse to launch in that case.
+  cudaFuncAttributes attr{};
+  if (cudaFuncGetAttributes(&attr, attn_fwd_kernel) != cudaSuccess ||
+      attr.numRegs != static_cast<int>(kRegsLaunch)) {
+    (void)cudaGetLastError();
+    return AVO_B200_ELAUNCH;
+  }
   if (dev < kMaxDevices) g_device_state[dev] = 1;
   return AVO_B200_OK;
 }

@@ -530,14 +530,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t v_smem = sRing + sv * kTileBytes;
         const uint32_t k_smem = sRing + sk * kTileBytes;
         released();  // V_j resident, keys 0-63 of P0_j published
-        AVO_TRACE_HOOK(2, j, 0);
         if (leader) issue_pv_half(tO0, tS0, v_smem, 0, j > 0 ? 1u : 0u);
         released();  // keys 64-127 of P0_j published
         if (leader) {
           issue_pv_half(tO0, tS0, v_smem, 1, 1u);
           mma_commit(bar(BAR_O_DONE + 0));
         }
-        AVO_TRACE_HOOK(2, j, 1);
         if (more) {
           released();  // K_{j+1} resident
           if (leader) {
@@ -545,9 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(bar(BAR_S_FULL + 0));
           }
         }
-        AVO_TRACE_HOOK(2, j, 2);
         released();  // keys 0-63 of P1_j published
-        AVO_TRACE_HOOK(2, j, 3);
         if (leader) issue_pv_half(tO1, tS1, v_smem, 0, j > 0 ? 1u : 0u);
         released();  // keys 64-127 of P1_j published
         if (leader) {
@@ -560,7 +556,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(bar(BAR_KV_EMPTY + sk));
           }
         }
-        AVO_TRACE_HOOK(2, j, 4);
       }
       __syncwarp();
       if (leader) {
@@ -591,19 +586,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tk = 2 * j + 2, sk = tk % kStages;
         if (lane == 0) {
           wait_phase(bar(BAR_KV_FULL + sv), (tv / kStages) & 1, watch);
+          AVO_TRACE_HOOK(2, j, 5);
           wait_phase(bar(BAR_P_HALF + 0), j & 1, watch);
+          AVO_TRACE_HOOK(2, j, 0);
         }
         release();
         if (lane == 0) wait_phase(bar(BAR_P_HALF + 1), j & 1, watch);
+        if (lane == 0) AVO_TRACE_HOOK(2, j, 1);
         release();
         if (j + 1 < n_tiles) {
           if (lane == 0) wait_phase(bar(BAR_KV_FULL + sk), (tk / kStages) & 1, watch);
+          if (lane == 0) AVO_TRACE_HOOK(2, j, 2);
           release();
         }
         if (lane == 0) wait_phase(bar(BAR_P_HALF + 2), j & 1, watch);
+        if (lane == 0) AVO_TRACE_HOOK(2, j, 3);
         release();
         if (lane == 0) wait_phase(bar(BAR_P_HALF + 3), j & 1, watch);
+        if (lane == 0) AVO_TRACE_HOOK(2, j, 4);
         release();
+        if (lane == 0) AVO_TRACE_HOOK(2, j, 6);
       }
     }
     __syncwarp();
