@@ -69,6 +69,9 @@ static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunc
 constexpr uint32_t kTmemCols = 512;            // S0 | S1 | O0 | O1, 128 columns each
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: rescale only past 2^8 growth
 constexpr int kEmuPairsPer8 = 2;               // FMA-pipe exp2 share: 2 of every 8 pairs
+constexpr int kSumAcc = 8;                     // independent packed row-sum accumulators
+
+constexpr uint32_t kWaitSuspendNs = 200000;   // try_wait suspend hint between watchdog checks
 
 // Device status bits (OR-ed into the caller's status word).
 constexpr int kStatusWatchdog = 1;  // a pipeline wait exceeded the watchdog; outputs invalid
@@ -118,11 +121,15 @@ struct Watch {
 // Waits for completion of phase `parity` of `bar`.  Returns false (and raises the
 // CTA abort flag plus the watchdog status bit) if the limit passes first, or at
 // once if another thread of the CTA already aborted.
+// The clock and the abort flag are read only every 64 probes, so a waiting warp
+// spends its issue slots on try_wait alone.
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const Watch& w) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+#pragma unroll 1
+    for (int probe = 0; probe < 64; ++probe)
+      if (mbar_try_wait(bar, parity)) return true;
     if (*w.abort) return false;
     if (global_timer_ns() - t0 > w.limit_ns) {
       *w.abort = 1;
@@ -135,7 +142,7 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const 
 // Bounded wait used only to drain work that is already in flight; ignores the abort flag.
 __device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity, const Watch& w) {
   const uint64_t t0 = global_timer_ns();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity, kWaitSuspendNs)) {
     if (global_timer_ns() - t0 > w.limit_ns) {
       if (w.status != nullptr) atomicOr(w.status, kStatusDrain);
       return;
@@ -180,7 +187,7 @@ __device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
 // interleave (MUFU and FMA chains side by side).
 template <bool kMix>
 __device__ __forceinline__ void exp_half(const uint32_t (&sa)[32], const uint32_t (&sb)[32],
-                                         uint64_t scale2, uint64_t neg_m2, uint64_t (&sum2)[2],
+                                         uint64_t scale2, uint64_t neg_m2, uint64_t (&sum2)[kSumAcc],
                                          uint32_t (&pk)[32]) {
 #pragma unroll
   for (int cc = 0; cc < 2; ++cc) {
@@ -196,7 +203,7 @@ __device__ __forceinline__ void exp_half(const uint32_t (&sa)[32], const uint32_
         p0 = ex2_approx(x0);
         p1 = ex2_approx(x1);
       }
-      sum2[(e >> 1) & 1] = f2_add(sum2[(e >> 1) & 1], f2_pack(p0, p1));
+      sum2[(e >> 1) % kSumAcc] = f2_add(sum2[(e >> 1) % kSumAcc], f2_pack(p0, p1));
       pk[cc * 16 + (e >> 1)] = pack_bf16x2(p0, p1);
     }
   }
@@ -322,7 +329,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool mix = !(tail || diag);
       const uint64_t scale2 = f2_pack(scale, scale);
       uint64_t neg_m2 = f2_pack((m == -CUDART_INF_F) ? 0.f : -m, (m == -CUDART_INF_F) ? 0.f : -m);
-      uint64_t sum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+      uint64_t sum2[kSumAcc];
+#pragma unroll
+      for (int q = 0; q < kSumAcc; ++q) sum2[q] = f2_pack(0.f, 0.f);
       uint32_t pk[32];
       if (mix) {
         exp_half<true>(s[0], s[1], scale2, neg_m2, sum2, pk);
@@ -351,8 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float neg_m = (m == -CUDART_INF_F) ? 0.f : -m;
         neg_m2 = f2_pack(neg_m, neg_m);
-        sum2[0] = f2_pack(0.f, 0.f);
-        sum2[1] = f2_pack(0.f, 0.f);
+#pragma unroll
+        for (int q = 0; q < kSumAcc; ++q) sum2[q] = f2_pack(0.f, 0.f);
         if (mix) {
           exp_half<true>(s[0], s[1], scale2, neg_m2, sum2, pk);
         } else {
@@ -398,10 +407,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(BAR_P_HALF + 2 * i + 1));
-      float a0, a1, b0, b1;
+#pragma unroll
+      for (int q = 1; q < kSumAcc; ++q) sum2[0] = f2_add(sum2[0], sum2[q]);
+      float a0, a1;
       f2_unpack(sum2[0], a0, a1);
-      f2_unpack(sum2[1], b0, b1);
-      l += (a0 + a1) + (b0 + b1);
+      l += a0 + a1;
       AVO_TRACE_HOOK(i, j, 4);
     }
 
