@@ -58,7 +58,7 @@ constexpr int kWaitWarp = 10;
 // Named barriers: 0 = __syncthreads, 1/2 = epilogue of softmax warpgroup 0/1,
 // 3 = waiter -> MMA warp release (64 threads).
 constexpr uint32_t kBarMmaHandoff = 3;
-constexpr int kThreads = 384;                  // 3 warpgroups: softmax 0, softmax 1, load/MMA
+constexpr int kThreads = 384;                  // 3 warpgroups: softmax 0, softmax 1, load/MMA/waiter
 // Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512), the
 // load/MMA warpgroup drops to 88 and each softmax warpgroup rises to 208:
 // 2 x 128 x 208 + 128 x 88 = 64512 (no spills in either role).
@@ -71,7 +71,7 @@ constexpr float kRescaleThreshold = 8.0f;      // log2 units: rescale only past 
 constexpr int kEmuPairsPer8 = 2;               // FMA-pipe exp2 share: 2 of every 8 pairs
 constexpr int kSumAcc = 8;                     // independent packed row-sum accumulators
 
-constexpr uint32_t kWaitSuspendNs = 200000;   // try_wait suspend hint between watchdog checks
+constexpr uint32_t kWaitSuspendNs = 200000;   // try_wait suspend hint while draining
 
 // Device status bits (OR-ed into the caller's status word).
 constexpr int kStatusWatchdog = 1;  // a pipeline wait exceeded the watchdog; outputs invalid
