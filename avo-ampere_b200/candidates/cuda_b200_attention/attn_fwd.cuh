@@ -181,11 +181,13 @@ __device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
 __device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
 
 // P for 64 keys (two 32-column chunks of S): x = s*scale - m by packed FMA, p = 2^x,
-// row sums accumulated in packed pairs, P packed to bf16x2 for tcgen05.st.  kMix
-// routes kEmuPairsPer8 of every 8 pairs through the FMA-pipe exp2; the choice is a
-// template parameter so each variant is straight-line code the compiler can
-// interleave (MUFU and FMA chains side by side).
-template <bool kMix>
+// row sums accumulated in packed pairs, P packed to bf16x2 for tcgen05.st.
+// kEmuPairsPer8 of every 8 pairs go through the FMA-pipe exp2 (exp2_poly_x2) to
+// offload the MUFU unit; the split is fixed at compile time, so the whole half is one
+// straight-line block in which MUFU and FMA chains interleave.  A masked (-inf) score
+// gives exactly 0 on the MUFU path and 2^-125 on the FMA path: negligible against any
+// row that sees a key (the row sum is >= 1), and a row that sees none is zeroed in
+// the epilogue.
 __device__ __forceinline__ void exp_half(const uint32_t (&sa)[32], const uint32_t (&sb)[32],
                                          uint64_t scale2, uint64_t neg_m2, uint64_t (&sum2)[kSumAcc],
                                          uint32_t (&pk)[32]) {
@@ -197,7 +199,7 @@ __device__ __forceinline__ void exp_half(const uint32_t (&sa)[32], const uint32_
       const uint64_t x2 = f2_fma(f2_pack(u2f(sc[e]), u2f(sc[e + 1])), scale2, neg_m2);
       float x0, x1, p0, p1;
       f2_unpack(x2, x0, x1);
-      if (kMix && ((e >> 1) & 7) < kEmuPairsPer8) {
+      if (((e >> 1) & 7) < kEmuPairsPer8) {
         exp2_poly_x2(f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f)), p0, p1);
       } else {
         p0 = ex2_approx(x0);
@@ -207,6 +209,40 @@ __device__ __forceinline__ void exp_half(const uint32_t (&sa)[32], const uint32_
       pk[cc * 16 + (e >> 1)] = pack_bf16x2(p0, p1);
     }
   }
+}
+
+// exp_half over keys 0-63 with the row max over all 128 scores (raw, unscaled) folded
+// into the same straight-line block: every pair step also folds two score pairs into
+// eight running maxima, so the independent max3 work fills the gaps between dependent
+// MUFU operations.  Measured on B200 with one warp per SM sub-partition: 565 cycles
+// for this half in one block, about 840 when a branch split the exps from a separate
+// max loop (the scheduler cannot interleave across basic blocks).
+__device__ __forceinline__ float exp_half_max(const uint32_t (&s)[4][32], uint64_t scale2, uint64_t neg_m2,
+                                              uint64_t (&sum2)[kSumAcc], uint32_t (&pk)[32]) {
+  float mx[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) mx[e] = -CUDART_INF_F;
+#pragma unroll
+  for (int q = 0; q < 32; ++q) {
+    const int cc = q >> 4, e = (q & 15) * 2;
+    const uint64_t x2 = f2_fma(f2_pack(u2f(s[cc][e]), u2f(s[cc][e + 1])), scale2, neg_m2);
+    float x0, x1, p0, p1;
+    f2_unpack(x2, x0, x1);
+    if ((q & 7) < kEmuPairsPer8) {
+      exp2_poly_x2(f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f)), p0, p1);
+    } else {
+      p0 = ex2_approx(x0);
+      p1 = ex2_approx(x1);
+    }
+    sum2[(q & 15) % kSumAcc] = f2_add(sum2[(q & 15) % kSumAcc], f2_pack(p0, p1));
+    pk[q] = pack_bf16x2(p0, p1);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int pr = 2 * q + r, c = pr >> 4, ee = (pr & 15) * 2;
+      mx[pr & 7] = fmax3(mx[pr & 7], u2f(s[c][ee]), u2f(s[c][ee + 1]));
+    }
+  }
+  return fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -326,27 +362,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // speculation almost always stands; when it does not (first tile, rare jumps)
       // the half is recomputed with the new max, giving exactly the values a
       // max-first order would.  An overflow of the speculative exp2 implies a move.
-      const bool mix = !(tail || diag);
       const uint64_t scale2 = f2_pack(scale, scale);
       uint64_t neg_m2 = f2_pack((m == -CUDART_INF_F) ? 0.f : -m, (m == -CUDART_INF_F) ? 0.f : -m);
       uint64_t sum2[kSumAcc];
 #pragma unroll
       for (int q = 0; q < kSumAcc; ++q) sum2[q] = f2_pack(0.f, 0.f);
       uint32_t pk[32];
-      if (mix) {
-        exp_half<true>(s[0], s[1], scale2, neg_m2, sum2, pk);
-      } else {
-        exp_half<false>(s[0], s[1], scale2, neg_m2, sum2, pk);
-      }
-      float mx[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) mx[e] = -CUDART_INF_F;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int e = 0; e < 32; e += 2)
-          mx[((c * 32 + e) >> 1) & 7] = fmax3(mx[((c * 32 + e) >> 1) & 7], u2f(s[c][e]), u2f(s[c][e + 1]));
-      const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+      const float mt = exp_half_max(s, scale2, neg_m2, sum2, pk);
       const float m_new = fmaxf(m, mt * scale);
       const bool grow = m_new > m + kRescaleThreshold;
       AVO_TRACE_HOOK(i, j, 2);
@@ -362,11 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         neg_m2 = f2_pack(neg_m, neg_m);
 #pragma unroll
         for (int q = 0; q < kSumAcc; ++q) sum2[q] = f2_pack(0.f, 0.f);
-        if (mix) {
-          exp_half<true>(s[0], s[1], scale2, neg_m2, sum2, pk);
-        } else {
-          exp_half<false>(s[0], s[1], scale2, neg_m2, sum2, pk);
-        }
+        exp_half(s[0], s[1], scale2, neg_m2, sum2, pk);
         if (j > 0) {
           // O holds P V summed over tiles < j relative to the old max.  The last of
           // those MMAs completed before S_j did (same issuing thread, in order);
@@ -387,20 +405,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       // Publish P in two 64-key halves, each as soon as it sits in TMEM, so PV on keys
-      // 0-63 overlaps the exps of keys 64-127.  On unmasked tiles kEmuPairsPer8 of
-      // every 8 pairs take the FMA-pipe exp2 (exp2_poly_x2) to offload the MUFU
-      // unit; masked tiles use ex2.approx only, which returns exactly 0 for masked
-      // (-inf) scores.
+      // 0-63 overlaps the exps of keys 64-127.
       tmem_st32(tS, pk);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(BAR_P_HALF + 2 * i + 0));
-      if (mix) {
-        exp_half<true>(s[2], s[3], scale2, neg_m2, sum2, pk);
-      } else {
-        exp_half<false>(s[2], s[3], scale2, neg_m2, sum2, pk);
-      }
+      exp_half(s[2], s[3], scale2, neg_m2, sum2, pk);
       AVO_TRACE_HOOK(i, j, 3);
       tmem_st32(tS + 32, pk);
       tc_wait_st();
@@ -421,7 +432,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // Epilogue: O / l -> bf16 -> swizzled stage in this tile's (now idle) Q buffer.
-    const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+    // A row that never saw a key keeps m = -inf (its l only holds the FMA-path exp2
+    // floor of masked scores): it gets O = 0 and LSE = -inf.  Once a row sees a key,
+    // the first rescale multiplies O and l by 2^(-inf) = 0, so no floor survives.
+    const bool seen = (m != -CUDART_INF_F) && (l > 0.f);
+    const float inv_l = seen ? 1.f / l : 0.f;
     uint8_t* stage = smem + kSmemQ + i * kTileBytes;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
@@ -446,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (p.lse != nullptr && row < p.seq_q) {
-      const float lse = (l > 0.f) ? (m + log2f(l)) * 0.69314718055994531f : -CUDART_INF_F;
+      const float lse = seen ? (m + log2f(l)) * 0.69314718055994531f : -CUDART_INF_F;
       p.lse[static_cast<long long>(bh) * p.lse_head_stride + row] = lse;
     }
     fence_proxy_async_smem();
