@@ -113,6 +113,17 @@ unsigned long long watchdog_limit_ns() {
   return limit;
 }
 
+// Test hook, read once per process: AVO_B200_TEST_SKIP_LOAD=n makes the producer skip its
+// n-th K/V copy (0-based, K_0 V_0 K_1 V_1 ...), so the wait for it runs out and the
+// launch exercises the kernel's watchdog abort path.  Unset (the default): -1, no skip.
+int test_skip_load() {
+  static const int skip = [] {
+    const char* env = std::getenv("AVO_B200_TEST_SKIP_LOAD");
+    return env ? std::atoi(env) : -1;
+  }();
+  return skip;
+}
+
 int resolve_encoder() {
   if (g_encode != nullptr) return AVO_B200_OK;
   void* fn = nullptr;
@@ -222,6 +233,7 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   p.q_pos0 = q_pos0;
   p.kv_pos0 = kv_pos0;
   p.watchdog_ns = watchdog_limit_ns();
+  p.test_skip_load = test_skip_load();
   p.seq_q = seq_q;
   p.seq_kv = seq_kv;
   p.num_bh = num_bh;

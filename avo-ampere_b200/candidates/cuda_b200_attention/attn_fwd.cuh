@@ -56,8 +56,11 @@ constexpr int kLoadWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kWaitWarp = 10;
 // Named barriers: 0 = __syncthreads, 1/2 = epilogue of softmax warpgroup 0/1,
-// 3 = waiter -> MMA warp release (64 threads).
+// 3 = waiter -> MMA warp release (64 threads), 4 + 2*tile + half = P half of a Q tile
+// published (the tile's 4 softmax warps arrive, the MMA warp syncs: 160 threads).
 constexpr uint32_t kBarMmaHandoff = 3;
+constexpr uint32_t kBarPHalf = 4;
+constexpr uint32_t kPHalfThreads = 128 + 32;
 constexpr int kThreads = 384;                  // 3 warpgroups: softmax 0, softmax 1, load/MMA/waiter
 // Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512), the
 // load/MMA warpgroup drops to 88 and each softmax warpgroup rises to 208:
@@ -86,8 +89,7 @@ enum : int {
   BAR_KV_FULL = 1,
   BAR_KV_EMPTY = BAR_KV_FULL + kStages,
   BAR_S_FULL = BAR_KV_EMPTY + kStages,
-  BAR_P_HALF = BAR_S_FULL + kQTiles,  // [2*tile + half]: P half published (one arrive per warp)
-  BAR_O_DONE = BAR_P_HALF + 2 * kQTiles,
+  BAR_O_DONE = BAR_S_FULL + kQTiles,
   BAR_DRAIN = BAR_O_DONE + kQTiles,
   NUM_BARS = BAR_DRAIN + 1
 };
@@ -110,6 +112,7 @@ struct AttnParams {
   int num_q_blocks;             // ceil(seq_q / 256)
   int causal;                   // key position > query position is masked
   float scale_log2;             // softmax_scale * log2(e)
+  int test_skip_load;           // test hook: K/V copy index the producer never issues, or -1
 };
 
 struct Watch {
@@ -140,10 +143,15 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const 
 }
 
 // Bounded wait used only to drain work that is already in flight; ignores the abort flag.
+// Its limit never drops below kDrainFloorNs, whatever the pipeline watchdog is set to:
+// copies and MMAs in flight land within microseconds, and a CTA must not exit while a
+// TMA copy can still write its shared memory.
+constexpr unsigned long long kDrainFloorNs = 100000000ull;  // 100 ms
 __device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity, const Watch& w) {
   const uint64_t t0 = global_timer_ns();
+  const unsigned long long limit = w.limit_ns > kDrainFloorNs ? w.limit_ns : kDrainFloorNs;
   while (!mbar_try_wait_sleep(bar, parity, kWaitSuspendNs)) {
-    if (global_timer_ns() - t0 > w.limit_ns) {
+    if (global_timer_ns() - t0 > limit) {
       if (w.status != nullptr) atomicOr(w.status, kStatusDrain);
       return;
     }
@@ -287,8 +295,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < kQTiles; ++i) {
       mbar_init(bar(BAR_S_FULL + i), 1);
-      mbar_init(bar(BAR_P_HALF + 2 * i + 0), kBlockM / 32);
-      mbar_init(bar(BAR_P_HALF + 2 * i + 1), kBlockM / 32);
       mbar_init(bar(BAR_O_DONE + i), 1);
     }
     mbar_init(bar(BAR_DRAIN), 1);
@@ -331,7 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l = 0.f;            // running sum of exp2(s*scale - m)
     bool ok = true;
 
-    for (int j = 0; j < n_tiles; ++j) {
+    int j = 0;
+    for (; j < n_tiles; ++j) {
       ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_S_FULL + i), j & 1, watch));
       if (!ok) break;
       AVO_TRACE_HOOK(i, j, 0);
@@ -405,25 +412,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       // Publish P in two 64-key halves, each as soon as it sits in TMEM, so PV on keys
-      // 0-63 overlaps the exps of keys 64-127.
+      // 0-63 overlaps the exps of keys 64-127.  The hand-off is a hardware named
+      // barrier the MMA warp syncs on (about 40 cycles, against about 130 for an
+      // mbarrier observed by a polling warp).
       tmem_st32(tS, pk);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(BAR_P_HALF + 2 * i + 0));
+      named_bar_arrive(kBarPHalf + 2 * i + 0, kPHalfThreads);
       exp_half(s[2], s[3], scale2, neg_m2, sum2, pk);
       AVO_TRACE_HOOK(i, j, 3);
       tmem_st32(tS + 32, pk);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(BAR_P_HALF + 2 * i + 1));
+      named_bar_arrive(kBarPHalf + 2 * i + 1, kPHalfThreads);
 #pragma unroll
       for (int q = 1; q < kSumAcc; ++q) sum2[0] = f2_add(sum2[0], sum2[q]);
       float a0, a1;
       f2_unpack(sum2[0], a0, a1);
       l += a0 + a1;
       AVO_TRACE_HOOK(i, j, 4);
+    }
+    // After a watchdog abort (which can only happen before a tile's first arrival) the
+    // MMA warp still runs its whole schedule, so this warp keeps its place in it: one
+    // arrival per half for every remaining tile.  These are blocking syncs, so an
+    // arrival can never run ahead into the next generation of a barrier.
+    for (; j < n_tiles; ++j) {
+      __syncwarp();
+      named_bar_sync(kBarPHalf + 2 * i + 0, kPHalfThreads);
+      named_bar_sync(kBarPHalf + 2 * i + 1, kPHalfThreads);
     }
 
     if (ok && n_tiles > 0) {
@@ -484,7 +502,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int h = 0; h < 2; ++h)
           tma_load_3d(sQ + i * kTileBytes + h * kHalfBytes, &tm_q, bar(BAR_Q), h * 64, q0 + i * kBlockM, bh,
                       pol_q);
-      int issued = 0;
+      // Per slot, 2 bits: bit 0 = a copy was issued into it, bit 1 = phase parity of the
+      // last one (all the abort drain needs; a register, not an indexed array).
+      uint32_t last_copy = 0;
       const int n_loads = 2 * n_tiles;
       for (int tt = 0; tt < min(kPrefetchAhead, n_loads); ++tt) {
         const CUtensorMap* tm = (tt & 1) ? &tm_v : &tm_k;
@@ -494,7 +514,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tt = 0; tt < n_loads; ++tt) {
         const int slot = tt % kStages;
         const int use = tt / kStages;
-        if (use > 0 && !wait_phase(bar(BAR_KV_EMPTY + slot), (use - 1) & 1, watch)) break;
+        if (use > 0) {
+          if (!wait_phase(bar(BAR_KV_EMPTY + slot), (use - 1) & 1, watch)) break;
+          // The previous copy into this slot has landed.  Always true once the MMA
+          // warp consumed it, except after an abort, when consumption no longer waits
+          // for data: this keeps at most one copy per slot in flight, so the drain
+          // below can name each slot's outstanding phase exactly.
+          if (!wait_phase(bar(BAR_KV_FULL + slot), (use - 1) & 1, watch)) break;
+        }
+        if (*abort_flag) break;
+        if (tt == p.test_skip_load) continue;  // test hook: this copy never arrives
         AVO_TRACE_HOOK(3, tt >> 1, tt & 1);
         mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), kTileBytes);
         const CUtensorMap* tm = (tt & 1) ? &tm_v : &tm_k;
@@ -502,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int h = 0; h < 2; ++h)
           tma_load_3d(sRing + slot * kTileBytes + h * kHalfBytes, tm, bar(BAR_KV_FULL + slot), h * 64, krow,
                       bh, pol_kv);
-        issued = tt + 1;
+        last_copy = (last_copy & ~(3u << (2 * slot))) | ((1u | ((use & 1u) << 1)) << (2 * slot));
         if (tt + kPrefetchAhead < n_loads) {
           const int pt = tt + kPrefetchAhead;
           const CUtensorMap* ptm = (pt & 1) ? &tm_v : &tm_k;
@@ -511,11 +540,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (*abort_flag) {
-        // Copies already issued still land in shared memory: wait for them.  Slot s
-        // last received copy number s + kStages * ((issued - 1 - s) / kStages).
+        // Copies already issued still land in shared memory: wait for them.  At most
+        // one copy per slot is ever in flight (see above), so each slot's outstanding
+        // phase is that of the last copy issued into it.
         drain_phase(bar(BAR_Q), 0, watch);
+#pragma unroll
         for (int s = 0; s < kStages; ++s)
-          if (issued > s) drain_phase(bar(BAR_KV_FULL + s), ((issued - 1 - s) / kStages) & 1, watch);
+          if ((last_copy >> (2 * s)) & 1u) drain_phase(bar(BAR_KV_FULL + s), (last_copy >> (2 * s + 1)) & 1u, watch);
       }
     }
     __syncwarp();
@@ -525,11 +556,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The whole warp runs the schedule and lane 0 issues.  It never reads shared
     // memory between MMA groups: on sm_100 any such read (an mbarrier wait included)
     // completes only after this thread's queued tcgen05.mma instructions have
-    // drained, leaving the tensor pipe idle while it refills.  Instead the waiter
-    // warp performs every mbarrier wait and releases this warp through a hardware
-    // named barrier, which does not drain the queue.  Both warps take the same
-    // number of rounds (a function of n_tiles only), including after a watchdog
-    // abort, so neither can be left waiting.
+    // drained, leaving the tensor pipe idle while it refills.  So it only ever waits
+    // on hardware named barriers, which do not drain the queue: the softmax
+    // warpgroups release it directly when a P half is in TMEM, and the waiter warp,
+    // which performs the K/V mbarrier waits, releases it when an operand tile is
+    // resident.  Every party takes a fixed number of rounds (a function of n_tiles
+    // only), including after a watchdog abort, so none can be left waiting.
     if (n_tiles > 0) {
       const bool leader = lane == 0;
       const uint32_t tS0 = tmem, tS1 = tmem + kBlockN;
@@ -538,6 +570,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto released = [&]() {
         __syncwarp();
         named_bar_sync(kBarMmaHandoff, 64);
+        tc_fence_after();
+      };
+      auto p_ready = [&](int tile, int half) {
+        __syncwarp();
+        named_bar_sync(kBarPHalf + 2 * tile + half, kPHalfThreads);
         tc_fence_after();
       };
       released();  // Q and K_0 resident
@@ -554,23 +591,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool more = j + 1 < n_tiles;
         const uint32_t v_smem = sRing + sv * kTileBytes;
         const uint32_t k_smem = sRing + sk * kTileBytes;
-        released();  // V_j resident, keys 0-63 of P0_j published
+        released();  // V_j resident
+        p_ready(0, 0);
         if (leader) issue_pv_half(tO0, tS0, v_smem, 0, j > 0 ? 1u : 0u);
-        released();  // keys 64-127 of P0_j published
+        if (more) released();  // K_{j+1} resident (taken here, off the P0 -> S0 path)
+        p_ready(0, 1);
         if (leader) {
           issue_pv_half(tO0, tS0, v_smem, 1, 1u);
           mma_commit(bar(BAR_O_DONE + 0));
-        }
-        if (more) {
-          released();  // K_{j+1} resident
-          if (leader) {
+          if (more) {
             issue_qk(tS0, sQ0, k_smem);
             mma_commit(bar(BAR_S_FULL + 0));
           }
         }
-        released();  // keys 0-63 of P1_j published
+        p_ready(1, 0);
         if (leader) issue_pv_half(tO1, tS1, v_smem, 0, j > 0 ? 1u : 0u);
-        released();  // keys 64-127 of P1_j published
+        p_ready(1, 1);
         if (leader) {
           issue_pv_half(tO1, tS1, v_smem, 1, 1u);
           mma_commit(bar(BAR_O_DONE + 1));
@@ -593,9 +629,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kWaitWarp) {
     regs_decrease<kRegsOther>();
     // ------------------------------------------------------------ waiter
-    // Performs, in the MMA warp's consumption order, every mbarrier wait that gates
-    // an MMA group, then releases the MMA warp (see above).  After an abort its
-    // waits return at once and it only keeps the round count.
+    // Performs, in the MMA warp's consumption order, the K/V mbarrier waits that gate
+    // its MMA groups and releases it for each (see above): Q and K_0, then per tile
+    // V_j and, if another tile follows, K_{j+1}.  After an abort its waits return at
+    // once and it only keeps the round count.
     if (n_tiles > 0) {
       auto release = [&]() {
         __syncwarp();
@@ -609,28 +646,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < n_tiles; ++j) {
         const int tv = 2 * j + 1, sv = tv % kStages;
         const int tk = 2 * j + 2, sk = tk % kStages;
-        if (lane == 0) {
-          wait_phase(bar(BAR_KV_FULL + sv), (tv / kStages) & 1, watch);
-          AVO_TRACE_HOOK(2, j, 5);
-          wait_phase(bar(BAR_P_HALF + 0), j & 1, watch);
-          AVO_TRACE_HOOK(2, j, 0);
-        }
-        release();
-        if (lane == 0) wait_phase(bar(BAR_P_HALF + 1), j & 1, watch);
-        if (lane == 0) AVO_TRACE_HOOK(2, j, 1);
+        if (lane == 0) wait_phase(bar(BAR_KV_FULL + sv), (tv / kStages) & 1, watch);
+        if (lane == 0) AVO_TRACE_HOOK(2, j, 5);
         release();
         if (j + 1 < n_tiles) {
           if (lane == 0) wait_phase(bar(BAR_KV_FULL + sk), (tk / kStages) & 1, watch);
           if (lane == 0) AVO_TRACE_HOOK(2, j, 2);
           release();
         }
-        if (lane == 0) wait_phase(bar(BAR_P_HALF + 2), j & 1, watch);
-        if (lane == 0) AVO_TRACE_HOOK(2, j, 3);
-        release();
-        if (lane == 0) wait_phase(bar(BAR_P_HALF + 3), j & 1, watch);
-        if (lane == 0) AVO_TRACE_HOOK(2, j, 4);
-        release();
-        if (lane == 0) AVO_TRACE_HOOK(2, j, 6);
       }
     }
     __syncwarp();
