@@ -10,6 +10,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <climits>
 #include <cmath>
 #include <cstdint>
@@ -262,6 +263,8 @@ extern "C" const char* avo_b200_strerror(int code) {
     case AVO_B200_ELAUNCH: return "CUDA launch error";
     case AVO_B200_ETENSORMAP: return "tensor map encoding failed";
     case AVO_B200_EDRIVER: return "driver entry point cuTensorMapEncodeTiled unavailable";
+    case AVO_B200_ETOOBIG:
+      return "problem too large for the no-allocation entry point (batch*heads*seq > 16384 rows)";
     default: return "unknown error";
   }
 }
@@ -338,4 +341,110 @@ extern "C" int avo_b200_watchdog_selftest(int timeout_us, int* status_dev, void*
   watchdog_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
       status_dev, static_cast<unsigned long long>(timeout_us) * 1000ull);
   return cudaGetLastError() == cudaSuccess ? AVO_B200_OK : AVO_B200_ELAUNCH;
+}
+
+// ---------------------------------------------------------------- no-allocation split path
+// Scratch of avo_b200_attn_fwd_split_noalloc, held statically on every device the library
+// runs on: a running fp32 accumulator (O and LSE) and one bf16/fp32 partial, each for up to
+// AVO_B200_NOALLOC_MAX_ROWS rows of 128 values.  About 12.1 MiB per device.
+static __device__ __align__(256) float g_noalloc_acc_o[AVO_B200_NOALLOC_MAX_ROWS * kHeadDim];
+static __device__ __align__(256) float g_noalloc_acc_lse[AVO_B200_NOALLOC_MAX_ROWS];
+static __device__ __align__(256) __nv_bfloat16 g_noalloc_part_o[AVO_B200_NOALLOC_MAX_ROWS * kHeadDim];
+static __device__ __align__(256) float g_noalloc_part_lse[AVO_B200_NOALLOC_MAX_ROWS];
+
+namespace avo_b200 {
+namespace noalloc {
+
+__global__ void fill_f32_kernel(float* __restrict__ p, float value, long long n) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = value;
+}
+
+struct NoAllocScratch {
+  float* acc_o;
+  float* acc_lse;
+  void* part_o;
+  float* part_lse;
+};
+
+// Device addresses of the static scratch, resolved with cudaGetSymbolAddress once per
+// device (the call needs the current device's context and costs a driver round trip).
+int noalloc_scratch(NoAllocScratch* out) {
+  static NoAllocScratch cache[kMaxDevices];
+  static bool ready[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    (void)cudaGetLastError();
+    return AVO_B200_ENODEV;
+  }
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!ready[dev]) {
+    NoAllocScratch s{};
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.acc_o), g_noalloc_acc_o) != cudaSuccess ||
+        cudaGetSymbolAddress(reinterpret_cast<void**>(&s.acc_lse), g_noalloc_acc_lse) != cudaSuccess ||
+        cudaGetSymbolAddress(&s.part_o, g_noalloc_part_o) != cudaSuccess ||
+        cudaGetSymbolAddress(reinterpret_cast<void**>(&s.part_lse), g_noalloc_part_lse) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return AVO_B200_ELAUNCH;
+    }
+    cache[dev] = s;
+    ready[dev] = true;
+  }
+  *out = cache[dev];
+  return AVO_B200_OK;
+}
+
+}  // namespace noalloc
+}  // namespace avo_b200
+
+extern "C" int avo_b200_attn_fwd_split_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
+                                                int batch, int heads, int seq, int head_dim, int causal,
+                                                float softmax_scale, int n_splits, int* status_dev,
+                                                void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr) return AVO_B200_EINVAL;
+  if (batch < 0 || heads < 0 || seq < 0 || head_dim != kHeadDim) return AVO_B200_EINVAL;
+  if (n_splits < 1 || n_splits > AVO_B200_NOALLOC_MAX_SPLITS) return AVO_B200_EINVAL;
+  if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale)) return AVO_B200_EINVAL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return AVO_B200_EINVAL;
+  if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u) != 0) return AVO_B200_EINVAL;
+  const long long bh = static_cast<long long>(batch) * heads;
+  const long long rows = bh * seq;
+  if (rows > AVO_B200_NOALLOC_MAX_ROWS) return AVO_B200_ETOOBIG;
+  if (rows == 0) return AVO_B200_OK;
+
+  int rc = prepare_device();
+  if (rc != AVO_B200_OK) return rc;
+  noalloc::NoAllocScratch s;
+  if ((rc = noalloc::noalloc_scratch(&s)) != AVO_B200_OK) return rc;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  // The accumulator starts empty: LSE = -inf (its O is then never read, see lse_merge).
+  noalloc::fill_f32_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(s.acc_lse, -INFINITY, rows);
+  if (cudaGetLastError() != cudaSuccess) return AVO_B200_ELAUNCH;
+
+  const int n_kv_tiles = (seq + kBlockN - 1) / kBlockN;
+  const int tiles_per_split = (n_kv_tiles + n_splits - 1) / n_splits;
+  const long long hs = static_cast<long long>(seq) * kHeadDim;
+  const int nbh = static_cast<int>(bh);
+  for (int sp = 0; sp < n_splits; ++sp) {
+    const long long k0 = static_cast<long long>(sp) * tiles_per_split * kBlockN;
+    if (k0 >= seq) break;
+    const int kv_len = static_cast<int>(std::min<long long>(seq - k0, static_cast<long long>(tiles_per_split) * kBlockN));
+    const size_t off = static_cast<size_t>(k0) * kHeadDim * sizeof(__nv_bfloat16);
+    // Keys [k0, k0 + kv_len) of every head; the causal mask uses their true positions.
+    rc = launch_fwd(q, static_cast<const char*>(k) + off, static_cast<const char*>(v) + off, s.part_o, s.part_lse,
+                    nbh, seq, kv_len, head_dim, hs, hs, hs, seq, causal, softmax_scale, 0, k0, status_dev, stream);
+    if (rc != AVO_B200_OK) return rc;
+    rc = avo_b200_lse_merge(s.acc_o, s.acc_lse, s.part_o, s.part_lse, nbh, seq, head_dim, hs, seq, hs, seq, stream);
+    if (rc != AVO_B200_OK) return rc;
+  }
+  rc = avo_b200_acc_to_bf16(s.acc_o, o, nbh, seq, head_dim, hs, hs, stream);
+  if (rc != AVO_B200_OK) return rc;
+  if (lse != nullptr &&
+      cudaMemcpyAsync(lse, s.acc_lse, static_cast<size_t>(rows) * sizeof(float), cudaMemcpyDeviceToDevice, st) !=
+          cudaSuccess) {
+    (void)cudaGetLastError();
+    return AVO_B200_ELAUNCH;
+  }
+  return AVO_B200_OK;
 }

@@ -44,11 +44,17 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     ),
     "avo_b200_acc_to_bf16": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_ll, _c_ll, _vp]),
     "avo_b200_watchdog_selftest": (_c_int, [_c_int, _vp, _vp]),
+    "avo_b200_attn_fwd_split_noalloc": (
+        _c_int,
+        [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp, _vp],
+    ),
 }
 ABI_VERSION = 1
 HEAD_DIM = 128
 STATUS_WATCHDOG = 1
 STATUS_DRAIN = 2
+NOALLOC_MAX_ROWS = 16384  # AVO_B200_NOALLOC_MAX_ROWS
+ETOOBIG = 6
 
 
 class B200AttentionError(RuntimeError):
@@ -195,6 +201,34 @@ def attention_forward(q, k, v, causal: bool, *, softmax_scale: float | None = No
             status_word(q.device).data_ptr(), _stream_handle(q.device),
         )
     _check(code, "avo_b200_attn_fwd")
+    return out, lse
+
+
+def attention_forward_noalloc(q, k, v, causal: bool, *, n_splits: int = 2, softmax_scale: float | None = None,
+                              need_lse: bool = True, out=None, lse=None):
+    """attention_forward through avo_b200_attn_fwd_split_noalloc: the key/value range in
+    n_splits blocks merged by log-sum-exp in the library's static scratch (no device
+    allocation by the library; B*H*S <= NOALLOC_MAX_ROWS).  Calls must not overlap in
+    time on one device: the scratch is shared."""
+    torch = _torch()
+    _validate(q, k, v)
+    batch, heads, seq, head_dim = (int(x) for x in q.shape)
+    if out is None:
+        out = torch.empty_like(q)
+    if need_lse and lse is None:
+        lse = torch.empty((batch, heads, seq), dtype=torch.float32, device=q.device)
+    if not need_lse:
+        lse = None
+    scale = default_scale(head_dim) if softmax_scale is None else float(softmax_scale)
+    lib = load_library()
+    with torch.cuda.device(q.device):
+        code = lib.avo_b200_attn_fwd_split_noalloc(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+            lse.data_ptr() if lse is not None else None,
+            batch, heads, seq, head_dim, 1 if causal else 0, scale, int(n_splits),
+            status_word(q.device).data_ptr(), _stream_handle(q.device),
+        )
+    _check(code, "avo_b200_attn_fwd_split_noalloc")
     return out, lse
 
 

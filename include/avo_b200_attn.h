@@ -22,6 +22,7 @@
  *   AVO_B200_ELAUNCH           3  CUDA reported an error at launch
  *   AVO_B200_ETENSORMAP        4  cuTensorMapEncodeTiled rejected a descriptor
  *   AVO_B200_EDRIVER           5  driver entry point for tensor maps unavailable
+ *   AVO_B200_ETOOBIG           6  problem exceeds the static scratch of the no-allocation entry
  *
  * Device status bits (written asynchronously into *status_dev when non-null; the
  * caller zeroes the word and reads it after synchronizing):
@@ -41,6 +42,11 @@ extern "C" {
 #define AVO_B200_ELAUNCH 3
 #define AVO_B200_ETENSORMAP 4
 #define AVO_B200_EDRIVER 5
+#define AVO_B200_ETOOBIG 6
+
+/* Row capacity (batch * heads * seq) of avo_b200_attn_fwd_split_noalloc's scratch. */
+#define AVO_B200_NOALLOC_MAX_ROWS 16384
+#define AVO_B200_NOALLOC_MAX_SPLITS 64
 
 #define AVO_B200_STATUS_WATCHDOG 1
 #define AVO_B200_STATUS_DRAIN 2
@@ -100,6 +106,25 @@ int avo_b200_lse_merge(float* acc_o, float* acc_lse, const void* part_o, const f
  */
 int avo_b200_acc_to_bf16(const float* acc_o, void* out, int num_bh, int rows, int head_dim,
                          long long acc_head_stride, long long out_head_stride, void* stream);
+
+/*
+ * Attention forward with the same arguments, layout and result as avo_b200_attn_fwd,
+ * computed as n_splits consecutive key/value blocks (whole 128-key tiles each) whose
+ * partial O and LSE are merged by log-sum-exp, using ONLY scratch the library holds in
+ * file-scope static device arrays: it allocates nothing (no cudaMalloc, no allocating
+ * library routine) and needs no workspace argument.  No counterpart in the reference.
+ *
+ * Limit: batch * heads * seq <= AVO_B200_NOALLOC_MAX_ROWS (16384 rows, about 12 MiB of
+ * static scratch per device); larger problems return AVO_B200_ETOOBIG before any device
+ * work.  1 <= n_splits <= AVO_B200_NOALLOC_MAX_SPLITS.  The scratch is shared by every
+ * caller on a device: calls that overlap in time (different streams, threads or
+ * processes' concurrent use of one library instance) race on it and must be
+ * serialized by the caller.  Partial results pass through bf16, so outputs may differ
+ * from avo_b200_attn_fwd by bf16 rounding.
+ */
+int avo_b200_attn_fwd_split_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
+                                    int batch, int heads, int seq, int head_dim, int causal,
+                                    float softmax_scale, int n_splits, int* status_dev, void* stream);
 
 /*
  * Self-test of the device watchdog without faulting the GPU: one CTA waits on an

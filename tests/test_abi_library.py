@@ -70,6 +70,16 @@ def test_host_side_argument_checks(b200):
     assert lib.avo_b200_lse_merge(None, None, None, None, 1, 1, 128, 128, 1, 128, 1, None) == 1
     assert lib.avo_b200_acc_to_bf16(fake, fake, 1, 4, 128, 100, 512, None) == 1
     assert lib.avo_b200_watchdog_selftest(0, fake, None) == 1
+    # The no-allocation entry point: argument errors, then a problem beyond its static
+    # scratch (16384 rows) is refused with its own code before any device work.
+    noalloc = lib.avo_b200_attn_fwd_split_noalloc
+    assert noalloc(None, fake, fake, fake, None, 1, 1, 128, 128, 0, 0.088, 2, None, None) == 1
+    assert noalloc(fake, fake, fake, fake, None, 1, 1, 128, 128, 0, 0.088, 0, None, None) == 1
+    assert noalloc(fake, fake, fake, fake, None, 1, 1, 128, 128, 0, 0.088, 65, None, None) == 1
+    assert noalloc(fake, fake, fake, fake, None, 1, 1, 16384 + 128, 128, 0, 0.088, 2, None, None) == 6
+    assert noalloc(fake, fake, fake, fake, None, 2, 16, 1024, 128, 0, 0.088, 2, None, None) == 6
+    assert noalloc(fake, fake, fake, fake, None, 0, 16, 1024, 128, 0, 0.088, 2, None, None) == 0
+    assert "too large" in b200.strerror(6)
 
 
 def test_no_gpu_means_enodev(b200):
