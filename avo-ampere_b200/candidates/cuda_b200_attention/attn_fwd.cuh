@@ -46,10 +46,6 @@ constexpr int kQTiles = 2;                     // Q tiles per CTA
 constexpr int kRowsPerCta = kBlockM * kQTiles; // 256
 constexpr int kBlockN = 128;                   // keys per K/V tile
 constexpr int kStages = 4;                     // K/V ring depth
-// K/V tiles are also prefetched into L2 this many ring positions ahead of their
-// shared-memory load: the CTAs that share a head reach each tile together, so
-// without it every tile's first touch pays full HBM latency inside the ring.
-constexpr int kPrefetchAhead = 8;
 constexpr int kTileBytes = 128 * kHeadDim * 2; // 32 KiB: 128 rows x 128 bf16
 constexpr int kHalfBytes = kTileBytes / 2;     // one 64-column, 128B-swizzled half
 constexpr int kLoadWarp = 8;
@@ -71,7 +67,9 @@ constexpr uint32_t kRegsOther = 88;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunch, "register split");
 constexpr uint32_t kTmemCols = 512;            // S0 | S1 | O0 | O1, 128 columns each
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: rescale only past 2^8 growth
-constexpr int kEmuPairsPer8 = 2;               // FMA-pipe exp2 share: 2 of every 8 pairs
+// FMA-pipe exp2 share: 1 of every 8 pairs (measured on B200 with this kernel: 1/8 beat
+// 0/8 by ~4 %, 2/8 by ~2.5 % and 3/8 by ~4 %).
+constexpr int kEmuPairsPer8 = 1;
 constexpr int kSumAcc = 8;                     // independent packed row-sum accumulators
 
 constexpr uint32_t kWaitSuspendNs = 200000;   // try_wait suspend hint while draining
@@ -506,11 +504,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // last one (all the abort drain needs; a register, not an indexed array).
       uint32_t last_copy = 0;
       const int n_loads = 2 * n_tiles;
-      for (int tt = 0; tt < min(kPrefetchAhead, n_loads); ++tt) {
-        const CUtensorMap* tm = (tt & 1) ? &tm_v : &tm_k;
-        tma_prefetch_3d(tm, 0, (tt >> 1) * kBlockN, bh);
-        tma_prefetch_3d(tm, 64, (tt >> 1) * kBlockN, bh);
-      }
+      // No separate L2 prefetch of K/V: measured on B200 it cost 1-2 % here (the prefetch
+      // operations share the TMA unit with the loads), the CTAs of a head reading the same
+      // tiles close together in time already hit L2.
       for (int tt = 0; tt < n_loads; ++tt) {
         const int slot = tt % kStages;
         const int use = tt / kStages;
@@ -532,12 +528,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(sRing + slot * kTileBytes + h * kHalfBytes, tm, bar(BAR_KV_FULL + slot), h * 64, krow,
                       bh, pol_kv);
         last_copy = (last_copy & ~(3u << (2 * slot))) | ((1u | ((use & 1u) << 1)) << (2 * slot));
-        if (tt + kPrefetchAhead < n_loads) {
-          const int pt = tt + kPrefetchAhead;
-          const CUtensorMap* ptm = (pt & 1) ? &tm_v : &tm_k;
-          tma_prefetch_3d(ptm, 0, (pt >> 1) * kBlockN, bh);
-          tma_prefetch_3d(ptm, 64, (pt >> 1) * kBlockN, bh);
-        }
       }
       if (*abort_flag) {
         // Copies already issued still land in shared memory: wait for them.  At most
