@@ -103,6 +103,7 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 EncodeTiledFn g_encode = nullptr;
 int g_device_state[kMaxDevices] = {};  // 0 unchecked, 1 ready, -1 not a B200
+int g_sm_count[kMaxDevices] = {};      // multiprocessors, read once per device
 
 unsigned long long watchdog_limit_ns() {
   static const unsigned long long limit = [] {
@@ -138,9 +139,9 @@ int resolve_encoder() {
   return AVO_B200_OK;
 }
 
-// Checks the current device once (compute capability 10.0) and raises the kernel's
-// dynamic shared-memory limit on it.
-int prepare_device() {
+// Checks the current device once (compute capability 10.0), raises the kernel's
+// dynamic shared-memory limit on it and reads its multiprocessor count (optional out).
+int prepare_device(int* sm_count = nullptr) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) {
     (void)cudaGetLastError();
@@ -149,7 +150,10 @@ int prepare_device() {
   std::lock_guard<std::mutex> lock(g_mu);
   const int rc = resolve_encoder();
   if (rc != AVO_B200_OK) return rc;
-  if (dev < kMaxDevices && g_device_state[dev] == 1) return AVO_B200_OK;
+  if (dev < kMaxDevices && g_device_state[dev] == 1) {
+    if (sm_count != nullptr) *sm_count = g_sm_count[dev];
+    return AVO_B200_OK;
+  }
   if (dev < kMaxDevices && g_device_state[dev] == -1) return AVO_B200_ENODEV;
   int major = 0, minor = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
@@ -175,7 +179,16 @@ int prepare_device() {
     (void)cudaGetLastError();
     return AVO_B200_ELAUNCH;
   }
-  if (dev < kMaxDevices) g_device_state[dev] = 1;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+    (void)cudaGetLastError();
+    return AVO_B200_ENODEV;
+  }
+  if (dev < kMaxDevices) {
+    g_sm_count[dev] = sms;
+    g_device_state[dev] = 1;
+  }
+  if (sm_count != nullptr) *sm_count = sms;
   return AVO_B200_OK;
 }
 
@@ -213,22 +226,28 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   if (lse != nullptr && lse_hs < seq_q) return AVO_B200_EINVAL;
   if (num_bh == 0 || seq_q == 0) return AVO_B200_OK;
 
-  int rc = prepare_device();
+  int sm_count = 0;
+  int rc = prepare_device(&sm_count);
   if (rc != AVO_B200_OK) return rc;
 
+  // Persistent grid: one CTA per multiprocessor (the kernel's shared memory admits one),
+  // each looping over 256-row query blocks.
   const int num_q_blocks = (seq_q + kRowsPerCta - 1) / kRowsPerCta;
-  const long long grid = static_cast<long long>(num_bh) * num_q_blocks;
-  if (grid > INT_MAX) return AVO_B200_EINVAL;
+  const long long items = static_cast<long long>(num_bh) * num_q_blocks;
+  if (items > INT_MAX) return AVO_B200_EINVAL;
+  const int grid = static_cast<int>(std::min<long long>(items, sm_count));
 
-  alignas(64) CUtensorMap tm_q, tm_k, tm_v, tm_o;
+  alignas(64) CUtensorMap tm_q, tm_k, tm_v;
   const int kv_rows = seq_kv > 0 ? seq_kv : 1;  // never read when seq_kv == 0
   if ((rc = encode_rows(&tm_q, q, seq_q, num_bh, q_hs)) != AVO_B200_OK) return rc;
   if ((rc = encode_rows(&tm_k, k, kv_rows, num_bh, kv_hs)) != AVO_B200_OK) return rc;
   if ((rc = encode_rows(&tm_v, v, kv_rows, num_bh, kv_hs)) != AVO_B200_OK) return rc;
-  if ((rc = encode_rows(&tm_o, o, seq_q, num_bh, o_hs)) != AVO_B200_OK) return rc;
 
   AttnParams p;
   p.lse = lse;
+  p.o = o;
+  p.o_head_stride = o_hs;
+  p.o_sector_aligned = ((reinterpret_cast<uintptr_t>(o) & 31u) == 0 && o_hs % 16 == 0) ? 1 : 0;
   p.status = status;
   p.lse_head_stride = lse_hs;
   p.q_pos0 = q_pos0;
@@ -243,7 +262,7 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   p.scale_log2 = scale * 1.4426950408889634f;
 
   attn_fwd_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
-      tm_q, tm_k, tm_v, tm_o, p);
+      tm_q, tm_k, tm_v, p);
   if (cudaGetLastError() != cudaSuccess) return AVO_B200_ELAUNCH;
   return AVO_B200_OK;
 }

@@ -8,19 +8,24 @@
 // recurrence of candidates/cuda_tiled_attention/attention_kernel.cu:84-99; the
 // structure is Blackwell-native and shares nothing with the reference kernels:
 //
-//   * one CTA owns 256 query rows of one (batch, head) as two 128-row Q tiles;
-//   * warp 8 streams K and V tiles (128 keys x 128 dims, bf16) with TMA into a
-//     4-slot shared-memory ring (K_j and V_j alternate), mbarrier-tracked;
+//   * the grid is persistent, one CTA per SM; a work item is 256 query rows of one
+//     (batch, head) as two 128-row Q tiles, and CTA c takes one item per wave,
+//     walking the waves in alternating directions (longest causal items first);
+//   * warp 8 streams Q and the K and V tiles (128 keys x 128 dims, bf16) with TMA:
+//     K_j and V_j alternate in a 4-slot shared-memory ring, mbarrier-tracked, and
+//     the next item's Q is loaded as soon as the current item's last S has read Q;
 //   * warp 9 issues tcgen05.mma: S_i = Q_i K_j^T into TMEM, then O_i += P_i V_j
-//     with P_i read straight from TMEM (it overwrites S_i as bf16);
+//     with P_i read straight from TMEM (it overwrites S_i as bf16); it waits only on
+//     hardware named barriers (warp 10 performs the mbarrier waits for it);
 //   * warps 0-3 and 4-7 are two softmax warpgroups, one per Q tile, one thread
 //     per query row: tcgen05.ld of the S row, max, exp2 with scale*log2(e) folded
 //     into one FFMA, row sum, tcgen05.st of P.  The running max is only raised
 //     when it grows by more than 2^8 ("conditional rescale"), so O in TMEM is
 //     rescaled rarely; the two groups ping-pong against the tensor core;
 //   * causal tiles above the diagonal are never loaded or multiplied;
-//   * the epilogue scales O by 1/l, stages it (swizzled) in the dead Q buffer and
-//     writes it with a TMA store; LSE (natural log) goes out as coalesced fp32.
+//   * the epilogue scales O by 1/l and writes each row straight from registers as
+//     whole 32-byte sectors, while the MMA warp already computes the next item's
+//     first S tiles; LSE (natural log) goes out as coalesced fp32.
 //
 // Every mbarrier wait is bounded by a wall-clock watchdog: on expiry the CTA sets
 // a status bit, stops issuing work, drains its in-flight copies and MMAs, frees
@@ -29,6 +34,8 @@
 
 #include <cuda_bf16.h>
 #include <math_constants.h>
+
+#include <type_traits>
 
 #include "sm100_ptx.cuh"
 
@@ -56,14 +63,15 @@ constexpr int kWaitWarp = 10;
 // published (the tile's 4 softmax warps arrive, the MMA warp syncs: 160 threads).
 constexpr uint32_t kBarMmaHandoff = 3;
 constexpr uint32_t kBarPHalf = 4;
+constexpr uint32_t kBarOFree = 8;  // 8 + tile: the tile's O read out by its epilogue (160 threads)
 constexpr uint32_t kPHalfThreads = 128 + 32;
 constexpr int kThreads = 384;                  // 3 warpgroups: softmax 0, softmax 1, load/MMA/waiter
 // Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512), the
 // load/MMA warpgroup drops to 88 and each softmax warpgroup rises to 208:
 // 2 x 128 x 208 + 128 x 88 = 64512 (no spills in either role).
 constexpr uint32_t kRegsLaunch = 168;
-constexpr uint32_t kRegsSoftmax = 208;
-constexpr uint32_t kRegsOther = 88;
+constexpr uint32_t kRegsSoftmax = 216;
+constexpr uint32_t kRegsOther = 72;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunch, "register split");
 constexpr uint32_t kTmemCols = 512;            // S0 | S1 | O0 | O1, 128 columns each
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: rescale only past 2^8 growth
@@ -84,7 +92,8 @@ constexpr int kSmemRing = kSmemQ + kQTiles * kTileBytes;
 constexpr int kSmemBars = kSmemRing + kStages * kTileBytes;
 enum : int {
   BAR_Q = 0,
-  BAR_KV_FULL = 1,
+  BAR_Q_EMPTY = 1,  // the current item's last S MMAs have read Q
+  BAR_KV_FULL = 2,
   BAR_KV_EMPTY = BAR_KV_FULL + kStages,
   BAR_S_FULL = BAR_KV_EMPTY + kStages,
   BAR_O_DONE = BAR_S_FULL + kQTiles,
@@ -108,6 +117,9 @@ struct AttnParams {
   int seq_kv;
   int num_bh;
   int num_q_blocks;             // ceil(seq_q / 256)
+  void* o;                      // bf16 output rows, [num_bh, o_head_stride]
+  int o_sector_aligned;         // o and o_head_stride * 2 bytes are multiples of 32
+  long long o_head_stride;      // elements between consecutive heads of o
   int causal;                   // key position > query position is masked
   float scale_log2;             // softmax_scale * log2(e)
   int test_skip_load;           // test hook: K/V copy index the producer never issues, or -1
@@ -158,28 +170,27 @@ __device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity, const
 
 // S = Q K^T for one 128x128 tile: 8 MMAs of K=16 along head_dim.  Both operands are
 // K-major, 128B-swizzled, stored as two 64-column halves of 128 rows.
-__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_smem, uint32_t k_smem) {
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_lo, uint32_t k_lo, uint32_t desc_hi) {
   constexpr uint32_t idesc = idesc_bf16_f32(kBlockM, kBlockN, 0, 0);
 #pragma unroll
   for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-    const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-    mma_ss(d_tmem, smem_desc_sw128(q_smem + off, 16, 1024), smem_desc_sw128(k_smem + off, 16, 1024),
-           idesc, kk > 0 ? 1u : 0u);
+    const uint32_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
+    mma_ss_lo(d_tmem, q_lo + off, k_lo + off, desc_hi, idesc, kk > 0 ? 1u : 0u);
   }
 }
 
 // O += P V over keys [64*half, 64*half + 64): P (128 rows x keys, bf16) from TMEM,
 // V (keys x 128 dims) from shared memory as an MN-major operand: dims contiguous, the
 // two 64-dim halves 16 KiB apart (leading byte offset), 8-key groups 1024 B apart
-// (stride byte offset).
-__device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_smem, int half,
-                                              uint32_t accumulate) {
+// (stride byte offset); v_lo = smem_desc_lo(V tile, 16 KiB).
+__device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_lo, uint32_t desc_hi,
+                                              int half, uint32_t accumulate) {
   constexpr uint32_t idesc = idesc_bf16_f32(kBlockM, kHeadDim, 0, 1);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const int kk = half * 4 + q;
-    mma_ts(d_tmem, p_tmem + kk * 8, smem_desc_sw128(v_smem + kk * 16 * 128, kHalfBytes, 1024), idesc,
-           (accumulate | (kk > 0 ? 1u : 0u)));
+    mma_ts_lo(d_tmem, p_tmem + kk * 8, v_lo + ((kk * 16 * 128) >> 4), desc_hi, idesc,
+              (accumulate | (kk > 0 ? 1u : 0u)));
   }
 }
 
@@ -251,10 +262,49 @@ __device__ __forceinline__ float exp_half_max(const uint32_t (&s)[4][32], uint64
   return fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
 }
 
+// Work item w (one CTA-sized block of 256 query rows of one head).  Causal grids run the
+// longest query blocks first.  n_tiles = KV tiles the block sees (0 if none).
+struct Item {
+  int bh, q0, n_tiles;
+};
+__device__ __forceinline__ Item item_at(int w, const AttnParams& p) {
+  int bh, qb;
+  if (p.causal) {
+    qb = p.num_q_blocks - 1 - w / p.num_bh;
+    bh = w % p.num_bh;
+  } else {
+    bh = w / p.num_q_blocks;
+    qb = w % p.num_q_blocks;
+  }
+  const int q0 = qb * kRowsPerCta;
+  const int n_kv_total = (p.seq_kv + kBlockN - 1) / kBlockN;
+  int n_tiles = n_kv_total;
+  if (p.causal) {
+    const long long q_last = p.q_pos0 + min(q0 + kRowsPerCta, p.seq_q) - 1;
+    const long long lim = q_last - p.kv_pos0;  // largest local key index any row may see
+    n_tiles = lim < 0 ? 0 : static_cast<int>(min(static_cast<long long>(n_kv_total), lim / kBlockN + 1));
+  }
+  return Item{bh, q0, n_tiles};
+}
+
+// Item of this CTA in wave r (gridDim.x items per wave): the CTAs walk the waves in
+// alternating directions, which balances the causal grid's decreasing item lengths
+// across CTAs as well as greedy list scheduling does.  May be >= the item count in
+// the last wave.
+__device__ __forceinline__ int wave_item(int r) {
+  return r * static_cast<int>(gridDim.x) +
+         ((r & 1) ? static_cast<int>(gridDim.x - 1 - blockIdx.x) : static_cast<int>(blockIdx.x));
+}
+
+// Persistent: each CTA processes one item per wave (wave_item).  Every role walks the same
+// sequence and derives all mbarrier phases from running counters (tiles, ring positions,
+// Q loads), so the pipeline flows from one item into the next: the producer loads the
+// next item's Q as soon as the current item's last S MMAs have read Q, and the MMA warp
+// computes the next item's first S tiles while the softmax warpgroups finish the current
+// item's epilogue.
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                    const AttnParams p) {
+                    const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
   extern __shared__ uint8_t smem_dyn[];
   const uint32_t raw = smem_addr(smem_dyn);
   uint8_t* smem = smem_dyn + ((1024u - (raw & 1023u)) & 1023u);
@@ -266,27 +316,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemAbort);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemTmemSlot);
   const Watch watch{abort_flag, p.status, p.watchdog_ns};
-
-  // Tile coordinates.  Causal grids run the longest query blocks first.
-  int bh, qb;
-  if (p.causal) {
-    qb = p.num_q_blocks - 1 - static_cast<int>(blockIdx.x / p.num_bh);
-    bh = static_cast<int>(blockIdx.x % p.num_bh);
-  } else {
-    bh = static_cast<int>(blockIdx.x / p.num_q_blocks);
-    qb = static_cast<int>(blockIdx.x % p.num_q_blocks);
-  }
-  const int q0 = qb * kRowsPerCta;
-  const int n_kv_total = (p.seq_kv + kBlockN - 1) / kBlockN;
-  int n_tiles = n_kv_total;
-  if (p.causal) {
-    const long long q_last = p.q_pos0 + min(q0 + kRowsPerCta, p.seq_q) - 1;
-    const long long lim = q_last - p.kv_pos0;  // largest local key index any row may see
-    n_tiles = lim < 0 ? 0 : static_cast<int>(min(static_cast<long long>(n_kv_total), lim / kBlockN + 1));
-  }
+  const int n_items = p.num_bh * p.num_q_blocks;
 
   if (threadIdx.x == 0) {
     mbar_init(bar(BAR_Q), 1);
+    mbar_init(bar(BAR_Q_EMPTY), 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(BAR_KV_FULL + s), 1);
       mbar_init(bar(BAR_KV_EMPTY + s), 1);
@@ -303,7 +337,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tm_q);
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
-    prefetch_tensormap(&tm_o);
   }
   if (warp == kMmaWarp) {
     tmem_alloc(smem_addr(tmem_slot), kTmemCols);
@@ -326,214 +359,272 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t tS = tmem + lane_off + i * kBlockN;
     const uint32_t tO = tmem + lane_off + 2 * kBlockN + i * kHeadDim;
-    const int row = q0 + i * kBlockM + t;
-    const long long qpos = p.q_pos0 + row;
-    const long long warp_qpos_min = p.q_pos0 + q0 + i * kBlockM + wq * 32;
     const float scale = p.scale_log2;
-
-    float m = -CUDART_INF_F;  // running max, log2 units (already scaled)
-    float l = 0.f;            // running sum of exp2(s*scale - m)
     bool ok = true;
-
-    int j = 0;
-    for (; j < n_tiles; ++j) {
-      ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_S_FULL + i), j & 1, watch));
-      if (!ok) break;
-      AVO_TRACE_HOOK(i, j, 0);
-      tc_fence_after();
-      uint32_t s[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_wait_ld(s[c]);
-      AVO_TRACE_HOOK(i, j, 1);
-
-      const int key_base = j * kBlockN;
-      const bool tail = key_base + kBlockN > p.seq_kv;
-      const bool diag = p.causal && (p.kv_pos0 + key_base + kBlockN - 1 > warp_qpos_min);
-      if (tail || diag) {
-        long long lim = p.seq_kv - key_base;
-        if (p.causal) lim = min(lim, qpos - (p.kv_pos0 + key_base) + 1);
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c * 32 + e >= lim) s[c][e] = f2u(-CUDART_INF_F);
+    // rg = 2 * wave + parity of the tiles of earlier items (the S_FULL / O_DONE phase
+    // base), one register for both.
+    for (int rg = 0; (rg >> 1) * static_cast<int>(gridDim.x) < n_items; rg += 2) {
+      const int r = rg >> 1;
+      const int w = wave_item(r);
+      if (w >= n_items) continue;
+      const Item it = item_at(w, p);
+      const int n_tiles = it.n_tiles;
+      // Visible keys as local key counts in [0, seq_kv]: this row sees keys [0, row_keys);
+      // every row of this warp sees at least the first warp_keys.
+      int row_keys = p.seq_kv, warp_keys = p.seq_kv;
+      if (p.causal) {
+        const long long rk = p.q_pos0 + it.q0 + i * kBlockM + t - p.kv_pos0 + 1;
+        const long long wk = p.q_pos0 + it.q0 + i * kBlockM + wq * 32 - p.kv_pos0 + 1;
+        row_keys = static_cast<int>(max(0LL, min(static_cast<long long>(p.seq_kv), rk)));
+        warp_keys = static_cast<int>(max(0LL, min(static_cast<long long>(p.seq_kv), wk)));
       }
 
-      // Speculative P for keys 0-63 against the running max, computed side by side
-      // with the row max over all 128 scores (independent instruction streams).  The
-      // running max only moves when the tile max exceeds it by more than 2^8, so the
-      // speculation almost always stands; when it does not (first tile, rare jumps)
-      // the half is recomputed with the new max, giving exactly the values a
-      // max-first order would.  An overflow of the speculative exp2 implies a move.
-      const uint64_t scale2 = f2_pack(scale, scale);
-      uint64_t neg_m2 = f2_pack((m == -CUDART_INF_F) ? 0.f : -m, (m == -CUDART_INF_F) ? 0.f : -m);
-      uint64_t sum2[kSumAcc];
-#pragma unroll
-      for (int q = 0; q < kSumAcc; ++q) sum2[q] = f2_pack(0.f, 0.f);
-      uint32_t pk[32];
-      const float mt = exp_half_max(s, scale2, neg_m2, sum2, pk);
-      const float m_new = fmaxf(m, mt * scale);
-      const bool grow = m_new > m + kRescaleThreshold;
-      AVO_TRACE_HOOK(i, j, 2);
+      float m = -CUDART_INF_F;  // running max, log2 units (already scaled)
+      float l = 0.f;            // running sum of exp2(s*scale - m)
 
-      if (__any_sync(0xffffffffu, grow)) {
-        float factor = 1.f;
-        if (grow) {
-          factor = ex2_approx(m - m_new);
-          l *= factor;
-          m = m_new;
+      int j = 0;
+      for (; ok && j < n_tiles; ++j) {
+        const int g = rg ^ j;  // parity of this tile's global index
+        ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_S_FULL + i), g & 1, watch));
+        if (!ok) break;
+        AVO_TRACE_HOOK(i, j, 0);
+        tc_fence_after();
+        uint32_t s[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_wait_ld(s[c]);
+        AVO_TRACE_HOOK(i, j, 1);
+
+        const int key_base = j * kBlockN;
+        if (key_base + kBlockN > warp_keys) {  // the tile has keys some row of this warp masks
+          const int lim = row_keys - key_base;
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (c * 32 + e >= lim) s[c][e] = f2u(-CUDART_INF_F);
         }
-        const float neg_m = (m == -CUDART_INF_F) ? 0.f : -m;
-        neg_m2 = f2_pack(neg_m, neg_m);
+
+        // Speculative P for keys 0-63 against the running max, computed side by side
+        // with the row max over all 128 scores (independent instruction streams).  The
+        // running max only moves when the tile max exceeds it by more than 2^8, so the
+        // speculation almost always stands; when it does not (first tile, rare jumps)
+        // the half is recomputed with the new max, giving exactly the values a
+        // max-first order would.  An overflow of the speculative exp2 implies a move.
+        const uint64_t scale2 = f2_pack(scale, scale);
+        uint64_t neg_m2 = f2_pack((m == -CUDART_INF_F) ? 0.f : -m, (m == -CUDART_INF_F) ? 0.f : -m);
+        uint64_t sum2[kSumAcc];
 #pragma unroll
         for (int q = 0; q < kSumAcc; ++q) sum2[q] = f2_pack(0.f, 0.f);
-        exp_half(s[0], s[1], scale2, neg_m2, sum2, pk);
-        if (j > 0) {
-          // O holds P V summed over tiles < j relative to the old max.  The last of
-          // those MMAs completed before S_j did (same issuing thread, in order);
-          // rescale this row in TMEM before any part of P_j is published.
-          ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (j - 1) & 1, watch));
-          if (!ok) break;
-          tc_fence_after();
+        uint32_t pk[32];
+        const float mt = exp_half_max(s, scale2, neg_m2, sum2, pk);
+        const float m_new = fmaxf(m, mt * scale);
+        const bool grow = m_new > m + kRescaleThreshold;
+        AVO_TRACE_HOOK(i, j, 2);
+
+        if (__any_sync(0xffffffffu, grow)) {
+          float factor = 1.f;
+          if (grow) {
+            factor = ex2_approx(m - m_new);
+            l *= factor;
+            m = m_new;
+          }
+          const float neg_m = (m == -CUDART_INF_F) ? 0.f : -m;
+          neg_m2 = f2_pack(neg_m, neg_m);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + c * 32, o);
-            tmem_wait_ld(o);
+          for (int q = 0; q < kSumAcc; ++q) sum2[q] = f2_pack(0.f, 0.f);
+          // Scores 0-63 again, from TMEM (S stays intact there until P is stored): then
+          // the registers of s[0] and s[1] need not outlive the speculative pass, which
+          // is the softmax warps' register peak.
+          uint32_t s01[2][32];
+          tmem_ld32(tS, s01[0]);
+          tmem_ld32(tS + 32, s01[1]);
+          tmem_wait_ld(s01[0]);
+          tmem_wait_ld(s01[1]);
+          if (key_base + kBlockN > warp_keys) {
+            const int lim = row_keys - key_base;
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = f2u(u2f(o[e]) * factor);
-            tmem_st32(tO + c * 32, o);
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                if (c * 32 + e >= lim) s01[c][e] = f2u(-CUDART_INF_F);
+          }
+          exp_half(s01[0], s01[1], scale2, neg_m2, sum2, pk);
+          if (j > 0) {
+            // O holds P V summed over tiles < j relative to the old max.  The last of
+            // those MMAs completed before S_j did (same issuing thread, in order);
+            // rescale this row in TMEM before any part of P_j is published.
+            ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (g - 1) & 1, watch));
+            if (!ok) break;
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              uint32_t o[32];
+              tmem_ld32(tO + c * 32, o);
+              tmem_wait_ld(o);
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = f2u(u2f(o[e]) * factor);
+              tmem_st32(tO + c * 32, o);
+            }
           }
         }
+
+        // Publish P in two 64-key halves, each as soon as it sits in TMEM, so PV on keys
+        // 0-63 overlaps the exps of keys 64-127.  The hand-off is a hardware named
+        // barrier the MMA warp syncs on (about 40 cycles, against about 130 for an
+        // mbarrier observed by a polling warp).
+        tmem_st32(tS, pk);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        named_bar_arrive(kBarPHalf + 2 * i + 0, kPHalfThreads);
+        exp_half(s[2], s[3], scale2, neg_m2, sum2, pk);
+        AVO_TRACE_HOOK(i, j, 3);
+        tmem_st32(tS + 32, pk);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        named_bar_arrive(kBarPHalf + 2 * i + 1, kPHalfThreads);
+#pragma unroll
+        for (int q = 1; q < kSumAcc; ++q) sum2[0] = f2_add(sum2[0], sum2[q]);
+        float a0, a1;
+        f2_unpack(sum2[0], a0, a1);
+        l += a0 + a1;
+        AVO_TRACE_HOOK(i, j, 4);
+      }
+      // After a watchdog abort (which can only happen before a tile's first arrival)
+      // the MMA warp still runs its whole schedule, so this warp keeps its place in it:
+      // one arrival per half for every remaining tile of every remaining item, and the
+      // O release of every item.  These are blocking syncs, so an arrival can never run
+      // ahead into the next generation of a barrier.
+      for (; j < n_tiles; ++j) {
+        __syncwarp();
+        named_bar_sync(kBarPHalf + 2 * i + 0, kPHalfThreads);
+        named_bar_sync(kBarPHalf + 2 * i + 1, kPHalfThreads);
       }
 
-      // Publish P in two 64-key halves, each as soon as it sits in TMEM, so PV on keys
-      // 0-63 overlaps the exps of keys 64-127.  The hand-off is a hardware named
-      // barrier the MMA warp syncs on (about 40 cycles, against about 130 for an
-      // mbarrier observed by a polling warp).
-      tmem_st32(tS, pk);
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      named_bar_arrive(kBarPHalf + 2 * i + 0, kPHalfThreads);
-      exp_half(s[2], s[3], scale2, neg_m2, sum2, pk);
-      AVO_TRACE_HOOK(i, j, 3);
-      tmem_st32(tS + 32, pk);
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      named_bar_arrive(kBarPHalf + 2 * i + 1, kPHalfThreads);
-#pragma unroll
-      for (int q = 1; q < kSumAcc; ++q) sum2[0] = f2_add(sum2[0], sum2[q]);
-      float a0, a1;
-      f2_unpack(sum2[0], a0, a1);
-      l += a0 + a1;
-      AVO_TRACE_HOOK(i, j, 4);
-    }
-    // After a watchdog abort (which can only happen before a tile's first arrival) the
-    // MMA warp still runs its whole schedule, so this warp keeps its place in it: one
-    // arrival per half for every remaining tile.  These are blocking syncs, so an
-    // arrival can never run ahead into the next generation of a barrier.
-    for (; j < n_tiles; ++j) {
-      __syncwarp();
-      named_bar_sync(kBarPHalf + 2 * i + 0, kPHalfThreads);
-      named_bar_sync(kBarPHalf + 2 * i + 1, kPHalfThreads);
-    }
-
-    if (ok && n_tiles > 0) {
-      ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (n_tiles - 1) & 1, watch));
-      tc_fence_after();
-    }
-
-    // Epilogue: O / l -> bf16 -> swizzled stage in this tile's (now idle) Q buffer.
-    // A row that never saw a key keeps m = -inf (its l only holds the FMA-path exp2
-    // floor of masked scores): it gets O = 0 and LSE = -inf.  Once a row sees a key,
-    // the first rescale multiplies O and l by 2^(-inf) = 0, so no floor survives.
-    const bool seen = (m != -CUDART_INF_F) && (l > 0.f);
-    const float inv_l = seen ? 1.f / l : 0.f;
-    uint8_t* stage = smem + kSmemQ + i * kTileBytes;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t o[32];
       if (ok && n_tiles > 0) {
-        tmem_ld32(tO + c * 32, o);
-        tmem_wait_ld(o);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] = 0u;
+        ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (rg ^ (n_tiles - 1)) & 1, watch));
+        tc_fence_after();
       }
-      uint8_t* rowp = stage + (c >> 1) * kHalfBytes + t * 128;
+
+      // Epilogue: O / l -> bf16 -> this thread's output row, written straight from
+      // registers as 8 whole 32-byte sectors (16-byte stores when o or its head stride is
+      // not 32-byte aligned; rows past seq_q are not written).  The Q buffer is not
+      // used for staging: the next item's Q may already be loading into it.  A row that
+      // never saw a key keeps m = -inf (its l only holds the FMA-path exp2 floor of
+      // masked scores): it gets O = 0 and LSE = -inf.  Once a row sees a key, the first
+      // rescale multiplies O and l by 2^(-inf) = 0, so no floor survives.
+      const bool seen = (m != -CUDART_INF_F) && (l > 0.f);
+      const float inv_l = seen ? 1.f / l : 0.f;
+      // (The item's head and rows are derived again here rather than kept in registers
+      // across the tile loop.)
+      const Item ie = item_at(wave_item(r), p);
+      const int row = ie.q0 + i * kBlockM + t;
+      const bool write = row < p.seq_q && *abort_flag == 0;
+      __nv_bfloat16* orow =
+          static_cast<__nv_bfloat16*>(p.o) + (static_cast<long long>(ie.bh) * p.o_head_stride +
+                                              static_cast<long long>(row) * kHeadDim);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 v;
-        v.x = pack_bf16x2(u2f(o[8 * q + 0]) * inv_l, u2f(o[8 * q + 1]) * inv_l);
-        v.y = pack_bf16x2(u2f(o[8 * q + 2]) * inv_l, u2f(o[8 * q + 3]) * inv_l);
-        v.z = pack_bf16x2(u2f(o[8 * q + 4]) * inv_l, u2f(o[8 * q + 5]) * inv_l);
-        v.w = pack_bf16x2(u2f(o[8 * q + 6]) * inv_l, u2f(o[8 * q + 7]) * inv_l);
-        const int chunk = ((c & 1) * 4 + q) ^ (t & 7);
-        *reinterpret_cast<uint4*>(rowp + chunk * 16) = v;
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        if (ok && n_tiles > 0) {
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld(o);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) w[e] = pack_bf16x2(u2f(o[2 * e]) * inv_l, u2f(o[2 * e + 1]) * inv_l);
+        if (write && p.o_sector_aligned) {
+          st_global_v8(orow + c * 32, w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7]);
+          st_global_v8(orow + c * 32 + 16, w[8], w[9], w[10], w[11], w[12], w[13], w[14], w[15]);
+        } else if (write) {
+          uint4* o16 = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) o16[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+        }
       }
-    }
-    if (p.lse != nullptr && row < p.seq_q) {
-      const float lse = seen ? (m + log2f(l)) * 0.69314718055994531f : -CUDART_INF_F;
-      p.lse[static_cast<long long>(bh) * p.lse_head_stride + row] = lse;
-    }
-    fence_proxy_async_smem();
-    named_bar_sync(1 + i, 128);
-    if (t == 0 && *abort_flag == 0) {
-      const uint32_t st = sQ + i * kTileBytes;
-      tma_store_3d(&tm_o, st, 0, q0 + i * kBlockM, bh);
-      tma_store_3d(&tm_o, st + kHalfBytes, 64, q0 + i * kBlockM, bh);
-      bulk_commit_group();
-      bulk_wait_group_read0();
+      if (n_tiles > 0) {
+        // O_i may now be overwritten by the next item's first PV.
+        tc_fence_before();
+        __syncwarp();
+        if (ok) {
+          named_bar_arrive(kBarOFree + i, kPHalfThreads);
+        } else {
+          named_bar_sync(kBarOFree + i, kPHalfThreads);
+        }
+      }
+      if (p.lse != nullptr && write) {
+        const float lse = seen ? (m + log2f(l)) * 0.69314718055994531f : -CUDART_INF_F;
+        p.lse[static_cast<long long>(ie.bh) * p.lse_head_stride + row] = lse;
+      }
+      rg ^= n_tiles & 1;
     }
   } else if (warp == kLoadWarp) {
     regs_decrease<kRegsOther>();
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && n_tiles > 0) {
+    if (lane == 0) {
       const uint64_t pol_q = policy_evict_first();
       const uint64_t pol_kv = policy_evict_last();
-      mbar_arrive_expect_tx(bar(BAR_Q), kQTiles * kTileBytes);
-      for (int i = 0; i < kQTiles; ++i)
-        for (int h = 0; h < 2; ++h)
-          tma_load_3d(sQ + i * kTileBytes + h * kHalfBytes, &tm_q, bar(BAR_Q), h * 64, q0 + i * kBlockM, bh,
-                      pol_q);
       // Per slot, 2 bits: bit 0 = a copy was issued into it, bit 1 = phase parity of the
       // last one (all the abort drain needs; a register, not an indexed array).
       uint32_t last_copy = 0;
-      const int n_loads = 2 * n_tiles;
+      int tt = 0;       // ring position (load order across items)
+      int nq = 0;       // Q loads issued (items with work)
+      bool stop = false;
       // No separate L2 prefetch of K/V: measured on B200 it cost 1-2 % here (the prefetch
       // operations share the TMA unit with the loads), the CTAs of a head reading the same
       // tiles close together in time already hit L2.
-      for (int tt = 0; tt < n_loads; ++tt) {
-        const int slot = tt % kStages;
-        const int use = tt / kStages;
-        if (use > 0) {
-          if (!wait_phase(bar(BAR_KV_EMPTY + slot), (use - 1) & 1, watch)) break;
-          // The previous copy into this slot has landed.  Always true once the MMA
-          // warp consumed it, except after an abort, when consumption no longer waits
-          // for data: this keeps at most one copy per slot in flight, so the drain
-          // below can name each slot's outstanding phase exactly.
-          if (!wait_phase(bar(BAR_KV_FULL + slot), (use - 1) & 1, watch)) break;
+      for (int r = 0; r * static_cast<int>(gridDim.x) < n_items && !stop; ++r) {
+        const int w = wave_item(r);
+        if (w >= n_items) continue;
+        const Item it = item_at(w, p);
+        if (it.n_tiles == 0) continue;
+        if (nq > 0) {
+          // The previous item's last S MMAs have read Q (committed to Q_EMPTY), and its
+          // Q load has landed (as for the K/V slots below: always true unless aborted).
+          if (!wait_phase(bar(BAR_Q_EMPTY), (nq - 1) & 1, watch)) break;
+          if (!wait_phase(bar(BAR_Q), (nq - 1) & 1, watch)) break;
         }
         if (*abort_flag) break;
-        if (tt == p.test_skip_load) continue;  // test hook: this copy never arrives
-        AVO_TRACE_HOOK(3, tt >> 1, tt & 1);
-        mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), kTileBytes);
-        const CUtensorMap* tm = (tt & 1) ? &tm_v : &tm_k;
-        const int krow = (tt >> 1) * kBlockN;
-        for (int h = 0; h < 2; ++h)
-          tma_load_3d(sRing + slot * kTileBytes + h * kHalfBytes, tm, bar(BAR_KV_FULL + slot), h * 64, krow,
-                      bh, pol_kv);
-        last_copy = (last_copy & ~(3u << (2 * slot))) | ((1u | ((use & 1u) << 1)) << (2 * slot));
+        mbar_arrive_expect_tx(bar(BAR_Q), kQTiles * kTileBytes);
+        for (int i = 0; i < kQTiles; ++i)
+          for (int h = 0; h < 2; ++h)
+            tma_load_3d(sQ + i * kTileBytes + h * kHalfBytes, &tm_q, bar(BAR_Q), h * 64, it.q0 + i * kBlockM,
+                        it.bh, pol_q);
+        ++nq;
+        for (int lt = 0; lt < 2 * it.n_tiles; ++lt, ++tt) {
+          const int slot = tt % kStages;
+          const int use = tt / kStages;
+          if (use > 0) {
+            if (!wait_phase(bar(BAR_KV_EMPTY + slot), (use - 1) & 1, watch)) { stop = true; break; }
+            // The previous copy into this slot has landed.  Always true once the MMA
+            // warp consumed it, except after an abort, when consumption no longer waits
+            // for data: this keeps at most one copy per slot in flight, so the drain
+            // below can name each slot's outstanding phase exactly.
+            if (!wait_phase(bar(BAR_KV_FULL + slot), (use - 1) & 1, watch)) { stop = true; break; }
+          }
+          if (*abort_flag) { stop = true; break; }
+          if (tt == p.test_skip_load) continue;  // test hook: this copy never arrives
+          AVO_TRACE_HOOK(3, lt >> 1, lt & 1);
+          mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), kTileBytes);
+          const CUtensorMap* tm = (lt & 1) ? &tm_v : &tm_k;
+          const int krow = (lt >> 1) * kBlockN;
+          for (int h = 0; h < 2; ++h)
+            tma_load_3d(sRing + slot * kTileBytes + h * kHalfBytes, tm, bar(BAR_KV_FULL + slot), h * 64, krow,
+                        it.bh, pol_kv);
+          last_copy = (last_copy & ~(3u << (2 * slot))) | ((1u | ((use & 1u) << 1)) << (2 * slot));
+        }
       }
       if (*abort_flag) {
         // Copies already issued still land in shared memory: wait for them.  At most
         // one copy per slot is ever in flight (see above), so each slot's outstanding
-        // phase is that of the last copy issued into it.
-        drain_phase(bar(BAR_Q), 0, watch);
+        // phase is that of the last copy issued into it; likewise the last Q load.
+        if (nq > 0) drain_phase(bar(BAR_Q), (nq - 1) & 1, watch);
 #pragma unroll
         for (int s = 0; s < kStages; ++s)
           if ((last_copy >> (2 * s)) & 1u) drain_phase(bar(BAR_KV_FULL + s), (last_copy >> (2 * s + 1)) & 1u, watch);
@@ -548,99 +639,154 @@ __global__ void __launch_bounds__(kThreads, 1)
     // completes only after this thread's queued tcgen05.mma instructions have
     // drained, leaving the tensor pipe idle while it refills.  So it only ever waits
     // on hardware named barriers, which do not drain the queue: the softmax
-    // warpgroups release it directly when a P half is in TMEM, and the waiter warp,
-    // which performs the K/V mbarrier waits, releases it when an operand tile is
-    // resident.  Every party takes a fixed number of rounds (a function of n_tiles
-    // only), including after a watchdog abort, so none can be left waiting.
-    if (n_tiles > 0) {
-      const bool leader = lane == 0;
-      const uint32_t tS0 = tmem, tS1 = tmem + kBlockN;
-      const uint32_t tO0 = tmem + 2 * kBlockN, tO1 = tO0 + kHeadDim;
-      const uint32_t sQ0 = sQ, sQ1 = sQ + kTileBytes;
-      auto released = [&]() {
-        __syncwarp();
-        named_bar_sync(kBarMmaHandoff, 64);
-        tc_fence_after();
-      };
-      auto p_ready = [&](int tile, int half) {
-        __syncwarp();
-        named_bar_sync(kBarPHalf + 2 * tile + half, kPHalfThreads);
-        tc_fence_after();
-      };
-      released();  // Q and K_0 resident
+    // warpgroups release it directly when a P half is in TMEM (and when an item's O
+    // has been read out), and the waiter warp, which performs the Q and K/V mbarrier
+    // waits, releases it when an operand tile is resident.  Every party takes a fixed
+    // number of rounds (a function of the item sequence only), including after a
+    // watchdog abort, so none can be left waiting.
+    const bool leader = lane == 0;
+    const uint32_t tS0 = tmem, tS1 = tmem + kBlockN;
+    const uint32_t tO0 = tmem + 2 * kBlockN, tO1 = tO0 + kHeadDim;
+    // Descriptor low words (smem_desc_lo): Q tiles, and ring slot 0 as a K (LBO 16 B) or
+    // V (LBO one 64-column half) operand; slot s adds s * kTileBytes / 16.
+    const uint32_t desc_hi = kDescHiSw128;
+    const uint32_t q0_lo = smem_desc_lo(sQ, 16), q1_lo = smem_desc_lo(sQ + kTileBytes, 16);
+    const uint32_t k_lo = smem_desc_lo(sRing, 16), v_lo = smem_desc_lo(sRing, kHalfBytes);
+    constexpr uint32_t kSlotLo = kTileBytes >> 4;
+    auto released = [&]() {
+      __syncwarp();
+      named_bar_sync(kBarMmaHandoff, 64);
+      tc_fence_after();
+    };
+    auto p_ready = [&](int tile, int half) {
+      __syncwarp();
+      named_bar_sync(kBarPHalf + 2 * tile + half, kPHalfThreads);
+      tc_fence_after();
+    };
+    auto o_free = [&](int tile) {
+      __syncwarp();
+      named_bar_sync(kBarOFree + tile, kPHalfThreads);
+      tc_fence_after();
+    };
+    // Every item loads 2 * n_tiles operands into the 4-slot ring, so each item's first K
+    // sits in slot 0 or 2: ring phase b.  Tile jj = j + b of an item then reads V from
+    // slot (2 jj + 1) % 4 and the next K from (2 jj + 2) % 4, exactly as if the item
+    // started the ring; the indices are a function of the loop counter alone, which
+    // keeps the issue code between barrier and MMA minimal.
+    int b = 0;
+    bool any = false;  // an item with work came before (its O must be released first)
+    for (int r = 0; r * static_cast<int>(gridDim.x) < n_items; ++r) {
+      const int w = wave_item(r);
+      if (w >= n_items) continue;
+      const int n_tiles = item_at(w, p).n_tiles;
+      if (n_tiles == 0) continue;
+      released();  // Q and K_0 of this item resident
       if (leader) {
-        issue_qk(tS0, sQ0, sRing);
+        const uint32_t k0 = k_lo + 2 * b * kSlotLo;
+        issue_qk(tS0, q0_lo, k0, desc_hi);
         mma_commit(bar(BAR_S_FULL + 0));
-        issue_qk(tS1, sQ1, sRing);
+        issue_qk(tS1, q1_lo, k0, desc_hi);
         mma_commit(bar(BAR_S_FULL + 1));
-        mma_commit(bar(BAR_KV_EMPTY + 0));
+        mma_commit(bar(BAR_KV_EMPTY + 2 * b));
+        if (n_tiles == 1) mma_commit(bar(BAR_Q_EMPTY));
       }
-      for (int j = 0; j < n_tiles; ++j) {
-        const int tv = 2 * j + 1, sv = tv % kStages;
-        const int tk = 2 * j + 2, sk = tk % kStages;
-        const bool more = j + 1 < n_tiles;
-        const uint32_t v_smem = sRing + sv * kTileBytes;
-        const uint32_t k_smem = sRing + sk * kTileBytes;
+      // Tile jj: PV for both Q tiles, and (kMore) the next tile's S as early as its P
+      // half allows.  The first tile of an item (kFirst) overwrites O, so it first waits
+      // until the previous item's epilogue has read O out.  First and last tiles are
+      // peeled off the loop, so the steady-state body carries no test at all.
+      auto tile = [&](int jj, auto first_tag, auto more_tag) {
+        constexpr bool kFirst = decltype(first_tag)::value;
+        constexpr bool kMore = decltype(more_tag)::value;
+        const uint32_t vj = v_lo + ((2 * jj + 1) % kStages) * kSlotLo;
+        const uint32_t kj = k_lo + ((2 * jj + 2) % kStages) * kSlotLo;
         released();  // V_j resident
+        if (kFirst && any) o_free(0);
         p_ready(0, 0);
-        if (leader) issue_pv_half(tO0, tS0, v_smem, 0, j > 0 ? 1u : 0u);
-        if (more) released();  // K_{j+1} resident (taken here, off the P0 -> S0 path)
+        if (leader) issue_pv_half(tO0, tS0, vj, desc_hi, 0, kFirst ? 0u : 1u);
+        if (kMore) released();  // K_{j+1} resident (taken here, off the P0 -> S0 path)
         p_ready(0, 1);
         if (leader) {
-          issue_pv_half(tO0, tS0, v_smem, 1, 1u);
+          issue_pv_half(tO0, tS0, vj, desc_hi, 1, 1u);
           mma_commit(bar(BAR_O_DONE + 0));
-          if (more) {
-            issue_qk(tS0, sQ0, k_smem);
+          if (kMore) {
+            issue_qk(tS0, q0_lo, kj, desc_hi);
             mma_commit(bar(BAR_S_FULL + 0));
           }
         }
+        if (kFirst && any) o_free(1);
         p_ready(1, 0);
-        if (leader) issue_pv_half(tO1, tS1, v_smem, 0, j > 0 ? 1u : 0u);
+        if (leader) issue_pv_half(tO1, tS1, vj, desc_hi, 0, kFirst ? 0u : 1u);
         p_ready(1, 1);
         if (leader) {
-          issue_pv_half(tO1, tS1, v_smem, 1, 1u);
+          issue_pv_half(tO1, tS1, vj, desc_hi, 1, 1u);
           mma_commit(bar(BAR_O_DONE + 1));
-          mma_commit(bar(BAR_KV_EMPTY + sv));
-          if (more) {
-            issue_qk(tS1, sQ1, k_smem);
+          mma_commit(bar(BAR_KV_EMPTY + (2 * jj + 1) % kStages));
+          if (kMore) {
+            issue_qk(tS1, q1_lo, kj, desc_hi);
             mma_commit(bar(BAR_S_FULL + 1));
-            mma_commit(bar(BAR_KV_EMPTY + sk));
+            mma_commit(bar(BAR_KV_EMPTY + (2 * jj + 2) % kStages));
           }
         }
+      };
+      using True = std::true_type;
+      using False = std::false_type;
+      if (n_tiles == 1) {
+        tile(b, True{}, False{});
+      } else {
+        tile(b, True{}, True{});
+        for (int jj = b + 1; jj < b + n_tiles - 1; ++jj) tile(jj, False{}, True{});
+        // Every S of this item has been issued: Q may be reloaded once they complete.
+        if (leader) mma_commit(bar(BAR_Q_EMPTY));
+        tile(b + n_tiles - 1, False{}, False{});
       }
-      __syncwarp();
-      if (leader) {
-        // Every MMA issued above completes before TMEM and shared memory are released.
-        mma_commit(bar(BAR_DRAIN));
-        drain_phase(bar(BAR_DRAIN), 0, watch);
-      }
+      b ^= n_tiles & 1;
+      any = true;
+    }
+    if (any) {
+      // The last item's O release (keeps the named barrier counts equal).
+      o_free(0);
+      o_free(1);
+    }
+    __syncwarp();
+    if (leader && any) {
+      // Every MMA issued above completes before TMEM and shared memory are released.
+      mma_commit(bar(BAR_DRAIN));
+      drain_phase(bar(BAR_DRAIN), 0, watch);
     }
     __syncwarp();
   } else if (warp == kWaitWarp) {
     regs_decrease<kRegsOther>();
     // ------------------------------------------------------------ waiter
-    // Performs, in the MMA warp's consumption order, the K/V mbarrier waits that gate
-    // its MMA groups and releases it for each (see above): Q and K_0, then per tile
-    // V_j and, if another tile follows, K_{j+1}.  After an abort its waits return at
-    // once and it only keeps the round count.
-    if (n_tiles > 0) {
-      auto release = [&]() {
-        __syncwarp();
-        named_bar_sync(kBarMmaHandoff, 64);
-      };
+    // Performs, in the MMA warp's consumption order, the Q and K/V mbarrier waits that
+    // gate its MMA groups and releases it for each (see above): per item Q and K_0,
+    // then per tile V_j and, if another tile follows, K_{j+1}.  After an abort its
+    // waits return at once and it only keeps the round count.
+    auto release = [&]() {
+      __syncwarp();
+      named_bar_sync(kBarMmaHandoff, 64);
+    };
+    int tt = 0;
+    int nq = 0;
+    for (int r = 0; r * static_cast<int>(gridDim.x) < n_items; ++r) {
+      const int w = wave_item(r);
+      if (w >= n_items) continue;
+      const int n_tiles = item_at(w, p).n_tiles;
+      if (n_tiles == 0) continue;
       if (lane == 0) {
-        wait_phase(bar(BAR_Q), 0, watch);
-        wait_phase(bar(BAR_KV_FULL + 0), 0, watch);
+        wait_phase(bar(BAR_Q), nq & 1, watch);
+        wait_phase(bar(BAR_KV_FULL + tt % kStages), (tt / kStages) & 1, watch);
       }
+      ++nq;
+      ++tt;
       release();
       for (int j = 0; j < n_tiles; ++j) {
-        const int tv = 2 * j + 1, sv = tv % kStages;
-        const int tk = 2 * j + 2, sk = tk % kStages;
-        if (lane == 0) wait_phase(bar(BAR_KV_FULL + sv), (tv / kStages) & 1, watch);
+        if (lane == 0) wait_phase(bar(BAR_KV_FULL + tt % kStages), (tt / kStages) & 1, watch);
+        ++tt;
         if (lane == 0) AVO_TRACE_HOOK(2, j, 5);
         release();
         if (j + 1 < n_tiles) {
-          if (lane == 0) wait_phase(bar(BAR_KV_FULL + sk), (tk / kStages) & 1, watch);
+          if (lane == 0) wait_phase(bar(BAR_KV_FULL + tt % kStages), (tt / kStages) & 1, watch);
+          ++tt;
           if (lane == 0) AVO_TRACE_HOOK(2, j, 2);
           release();
         }
