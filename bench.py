@@ -76,6 +76,7 @@ def profiled_traffic(workload: str) -> float | None:
     if not path.is_file():
         return None
     for line in path.read_text().splitlines():
+        line = line.strip()
         if line.startswith("dram_bytes_per_launch:"):
             try:
                 return float(line.split(":", 1)[1].strip())
