@@ -361,10 +361,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tO = tmem + lane_off + 2 * kBlockN + i * kHeadDim;
     const float scale = p.scale_log2;
     bool ok = true;
-    // rg = 2 * wave + parity of the tiles of earlier items (the S_FULL / O_DONE phase
-    // base), one register for both.
-    for (int rg = 0; (rg >> 1) * static_cast<int>(gridDim.x) < n_items; rg += 2) {
-      const int r = rg >> 1;
+    // rg = 4 * wave + 2 * parity of the earlier items with work (the O_DONE phase) +
+    // parity of their tiles (the S_FULL phase base), one register for all three.
+    for (int rg = 0; (rg >> 2) * static_cast<int>(gridDim.x) < n_items; rg += 4) {
+      const int r = rg >> 2;
       const int w = wave_item(r);
       if (w >= n_items) continue;
       const Item it = item_at(w, p);
@@ -452,12 +452,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           exp_half(s01[0], s01[1], scale2, neg_m2, sum2, pk);
           if (j > 0) {
-            // O holds P V summed over tiles < j relative to the old max.  The last of
-            // those MMAs completed before S_j did (same issuing thread, in order);
-            // rescale this row in TMEM before any part of P_j is published.
-            ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (g - 1) & 1, watch));
-            if (!ok) break;
-            tc_fence_after();
+            // O holds P V summed over tiles < j relative to the old max; rescale this
+            // row in TMEM before any part of P_j is published.  Those MMAs are complete:
+            // the S_j commit just observed was issued after them by the same thread,
+            // and a commit tracks every earlier MMA of its thread.
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               uint32_t o[32];
@@ -505,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       if (ok && n_tiles > 0) {
-        ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (rg ^ (n_tiles - 1)) & 1, watch));
+        ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (rg >> 1) & 1, watch));
         tc_fence_after();
       }
 
@@ -562,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float lse = seen ? (m + log2f(l)) * 0.69314718055994531f : -CUDART_INF_F;
         p.lse[static_cast<long long>(ie.bh) * p.lse_head_stride + row] = lse;
       }
-      rg ^= n_tiles & 1;
+      if (n_tiles > 0) rg ^= 2 | (n_tiles & 1);
     }
   } else if (warp == kLoadWarp) {
     regs_decrease<kRegsOther>();
@@ -707,7 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         p_ready(0, 1);
         if (leader) {
           issue_pv_half(tO0, tS0, vj, desc_hi, 1, 1u);
-          mma_commit(bar(BAR_O_DONE + 0));
+          if (!kMore) mma_commit(bar(BAR_O_DONE + 0));  // the item's O_0 is complete
           if (kMore) {
             issue_qk(tS0, q0_lo, kj, desc_hi);
             mma_commit(bar(BAR_S_FULL + 0));
@@ -719,7 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         p_ready(1, 1);
         if (leader) {
           issue_pv_half(tO1, tS1, vj, desc_hi, 1, 1u);
-          mma_commit(bar(BAR_O_DONE + 1));
+          if (!kMore) mma_commit(bar(BAR_O_DONE + 1));
           mma_commit(bar(BAR_KV_EMPTY + (2 * jj + 1) % kStages));
           if (kMore) {
             issue_qk(tS1, q1_lo, kj, desc_hi);
