@@ -115,8 +115,9 @@ unsigned long long watchdog_limit_ns() {
   return limit;
 }
 
-// Test hook, read once per process: AVO_B200_TEST_SKIP_LOAD=n makes the producer skip its
-// n-th K/V copy (0-based, K_0 V_0 K_1 V_1 ...), so the wait for it runs out and the
+// Test hook, read once per process: AVO_B200_TEST_SKIP_LOAD=n makes each CTA's producer
+// skip its n-th K/V copy (0-based, counted over the CTA's work items in order: K_0 V_0
+// K_1 V_1 ... of its first item, then of its next), so the wait for it runs out and the
 // launch exercises the kernel's watchdog abort path.  Unset (the default): -1, no skip.
 int test_skip_load() {
   static const int skip = [] {
