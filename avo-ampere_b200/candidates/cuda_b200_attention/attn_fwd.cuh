@@ -49,8 +49,8 @@ namespace avo_b200 {
 
 constexpr int kHeadDim = 128;
 constexpr int kBlockM = 128;                   // rows per Q tile (one M=128 accumulator)
-constexpr int kQTiles = 2;                     // Q tiles per CTA
-constexpr int kRowsPerCta = kBlockM * kQTiles; // 256
+constexpr int kQTiles = 2;                     // Q tiles per work item
+constexpr int kRowsPerCta = kBlockM * kQTiles; // 256 query rows per work item
 constexpr int kBlockN = 128;                   // keys per K/V tile
 constexpr int kStages = 4;                     // K/V ring depth
 constexpr int kTileBytes = 128 * kHeadDim * 2; // 32 KiB: 128 rows x 128 bf16
@@ -58,25 +58,27 @@ constexpr int kHalfBytes = kTileBytes / 2;     // one 64-column, 128B-swizzled h
 constexpr int kLoadWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kWaitWarp = 10;
-// Named barriers: 0 = __syncthreads, 1/2 = epilogue of softmax warpgroup 0/1,
-// 3 = waiter -> MMA warp release (64 threads), 4 + 2*tile + half = P half of a Q tile
-// published (the tile's 4 softmax warps arrive, the MMA warp syncs: 160 threads).
+// Named barriers: 0 = __syncthreads, 3 = waiter -> MMA warp release (64 threads),
+// 4 + 2*tile + half = P half of a Q tile published, 8 + tile = the tile's O read out by
+// its epilogue (for both: the tile's 4 softmax warps arrive, the MMA warp syncs; 160
+// threads).
 constexpr uint32_t kBarMmaHandoff = 3;
 constexpr uint32_t kBarPHalf = 4;
-constexpr uint32_t kBarOFree = 8;  // 8 + tile: the tile's O read out by its epilogue (160 threads)
+constexpr uint32_t kBarOFree = 8;
 constexpr uint32_t kPHalfThreads = 128 + 32;
 constexpr int kThreads = 384;                  // 3 warpgroups: softmax 0, softmax 1, load/MMA/waiter
 // Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512), the
-// load/MMA warpgroup drops to 88 and each softmax warpgroup rises to 208:
-// 2 x 128 x 208 + 128 x 88 = 64512 (no spills in either role).
+// load/MMA warpgroup drops to 72 and each softmax warpgroup rises to 216:
+// 2 x 128 x 216 + 128 x 72 = 64512 (no spills in either role; measured on B200 against
+// 208/88: equal or up to 3 % faster).
 constexpr uint32_t kRegsLaunch = 168;
 constexpr uint32_t kRegsSoftmax = 216;
 constexpr uint32_t kRegsOther = 72;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunch, "register split");
 constexpr uint32_t kTmemCols = 512;            // S0 | S1 | O0 | O1, 128 columns each
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: rescale only past 2^8 growth
-// FMA-pipe exp2 share: 1 of every 8 pairs (measured on B200 with this kernel: 1/8 beat
-// 0/8 by ~4 %, 2/8 by ~2.5 % and 3/8 by ~4 %).
+// FMA-pipe exp2 share: 1 of every 8 pairs (measured on B200: 1/8 beat 0/8 by 4-7 % and
+// 3/8 by ~4 %; 2/8 is within noise of it).
 constexpr int kEmuPairsPer8 = 1;
 constexpr int kSumAcc = 8;                     // independent packed row-sum accumulators
 
@@ -384,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       int j = 0;
       for (; ok && j < n_tiles; ++j) {
-        const int g = rg ^ j;  // parity of this tile's global index
+        const int g = rg ^ j;  // bit 0: parity of this tile's index over the CTA's items
         ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_S_FULL + i), g & 1, watch));
         if (!ok) break;
         AVO_TRACE_HOOK(i, j, 0);
