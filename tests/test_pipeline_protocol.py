@@ -317,3 +317,13 @@ def test_protocol_random_item_sequences():
 def test_planted_mistakes_are_caught(fault):
     caught = any(run_model([4, 4, 3], 1, seed, fault) for seed in range(25))
     assert caught, fault
+
+
+@pytest.mark.parametrize("n_items,grid", [(1, 1), (7, 3), (148, 148), (1024, 148), (600, 148), (1000, 7)])
+def test_wave_order_visits_every_item_once(n_items, grid):
+    # wave_item(r) of attn_fwd.cuh: CTA c takes r*G + c on even waves, r*G + G-1-c on odd ones.
+    seen = sorted(w for seq in cta_sequences(list(range(n_items)), grid) for w in seq)
+    assert seen == list(range(n_items))
+    # and the CTAs' totals differ by at most one item
+    counts = [len(seq) for seq in cta_sequences(list(range(n_items)), grid)]
+    assert max(counts) - min(counts) <= 1
