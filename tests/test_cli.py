@@ -2,8 +2,6 @@
 
 from __future__ import annotations
 
-from pathlib import Path
-
 import pytest
 
 from avo.cli import build_parser, parse_ncu_raw_csv, profile_command, worker_argv

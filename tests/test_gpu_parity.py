@@ -9,7 +9,6 @@ scorer's gate torch.allclose(atol=3e-2, rtol=3e-2) (avo/benchmark.py:638-639).
 from __future__ import annotations
 
 import importlib.util
-import sys
 
 import numpy as np
 import pytest
