@@ -70,7 +70,7 @@ constexpr int kThreads = 384;                  // 3 warpgroups: softmax 0, softm
 // Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512), the
 // load/MMA warpgroup drops to 72 and each softmax warpgroup rises to 216:
 // 2 x 128 x 216 + 128 x 72 = 64512 (no spills in either role; measured on B200 against
-// 208/88: equal or up to 3 % faster).
+// 208/88 and 224/56: equal on non-causal work, faster on causal).
 constexpr uint32_t kRegsLaunch = 168;
 constexpr uint32_t kRegsSoftmax = 216;
 constexpr uint32_t kRegsOther = 72;
