@@ -1,15 +1,15 @@
 """CUDA toolchain environment and the B200 hardware check.
 
-Mirror of the reference's ``avo/cuda_env.py`` (``prepare_torch_extension_env`` :31-46,
-``nvcc_cuda_version`` / ``parse_nvcc_release`` :111-146, ``cuda_build_compatibility``
-:149-175) retargeted to the B200:
+Serves the same callers as the reference's ``avo/cuda_env.py`` (the CLI's ``env`` report
+and the environment handed to build workers), retargeted to the B200:
 
-* the torch-extension arch list becomes ``10.0a`` (the reference pins ``8.6``, :37);
+* the torch-extension arch list is ``10.0a`` (the reference pins ``8.6``);
 * ``check_b200`` / ``require_b200`` replace the scorer's sm_86 assertion with a check
   for compute capability 10.0;
-* ``library_build_compatibility`` states the rule for the candidate's C-ABI library:
-  it links the CUDA runtime statically, so it needs only a driver at least as new as
-  the nvcc that built it (not a torch-matching toolkit).
+* the toolkit probe reports nvcc's path and release in one record, and two rules say
+  whether a build can work: a torch extension wants nvcc's major version to match
+  torch's CUDA, while the candidate's C-ABI library links the CUDA runtime statically
+  and only needs a driver at least as new as the nvcc that built it.
 """
 
 from __future__ import annotations
@@ -19,93 +19,94 @@ import re
 import shutil
 import subprocess
 from collections.abc import MutableMapping
+from dataclasses import dataclass
 from pathlib import Path
 from typing import Any
 
 from .config import ACTIVE_TARGET
 
 DEFAULT_CUDA_HOME = "/usr/local/cuda"
+_VERSION_RE = re.compile(r"(\d+)\.(\d+)")
 
 
 def prepare_torch_extension_env(env: MutableMapping[str, str] | None = None, *,
                                 max_jobs: str = "2") -> MutableMapping[str, str]:
+    """Fill in the build variables a worker needs, keeping any the caller set."""
     target = os.environ if env is None else env
-    target.setdefault("TORCH_CUDA_ARCH_LIST", ACTIVE_TARGET.torch_arch_list)
-    target.setdefault("MAX_JOBS", max_jobs)
-    if "CUDA_HOME" not in target and (Path(DEFAULT_CUDA_HOME) / "bin" / "nvcc").exists():
-        target["CUDA_HOME"] = DEFAULT_CUDA_HOME
+    defaults = {"TORCH_CUDA_ARCH_LIST": ACTIVE_TARGET.torch_arch_list, "MAX_JOBS": max_jobs}
+    if Path(DEFAULT_CUDA_HOME, "bin", "nvcc").exists():
+        defaults["CUDA_HOME"] = DEFAULT_CUDA_HOME
+    for key, value in defaults.items():
+        if key not in target:
+            target[key] = value
     return target
 
 
-def nvcc_path_from_env(env: dict[str, str]) -> str | None:
-    cuda_home = env.get("CUDA_HOME") or env.get("CUDA_PATH")
-    if cuda_home:
-        return str(Path(cuda_home) / "bin" / "nvcc")
+def version_tuple(text: str | None) -> tuple[int, int] | None:
+    """(major, minor) of the first ``X.Y`` in ``text``."""
+    if not text:
+        return None
+    found = _VERSION_RE.search(text)
+    return (int(found.group(1)), int(found.group(2))) if found else None
+
+
+@dataclass(frozen=True)
+class NvccProbe:
+    path: str | None
+    release: str | None  # "12.9"
+    error: str | None
+
+
+def find_nvcc(env: MutableMapping[str, str]) -> str | None:
+    """nvcc under CUDA_HOME (or CUDA_PATH) if either is set, else the first on PATH."""
+    for key in ("CUDA_HOME", "CUDA_PATH"):
+        if env.get(key):
+            return os.path.join(env[key], "bin", "nvcc")
     return shutil.which("nvcc", path=env.get("PATH"))
+
+
+def probe_nvcc(env: MutableMapping[str, str]) -> NvccProbe:
+    """Run ``nvcc --version`` and read its ``release X.Y``."""
+    path = find_nvcc(env)
+    if path is None:
+        return NvccProbe(None, None, "no nvcc under CUDA_HOME/CUDA_PATH or on PATH")
+    try:
+        proc = subprocess.run([path, "--version"], capture_output=True, text=True, env=dict(env),
+                              timeout=10)
+    except (OSError, subprocess.TimeoutExpired) as exc:
+        return NvccProbe(path, None, f"{path} --version: {type(exc).__name__}: {exc}")
+    text = proc.stdout + "\n" + proc.stderr
+    if proc.returncode != 0:
+        return NvccProbe(path, None, f"{path} --version exited {proc.returncode}: {text.strip()[:200]}")
+    release = re.search(r"release\s+(\d+\.\d+)", text)
+    if release is None:
+        return NvccProbe(path, None, f"no 'release X.Y' in the output of {path} --version")
+    return NvccProbe(path, release.group(1), None)
 
 
 def torch_cuda_version() -> str | None:
     try:
         import torch
-    except Exception:
+    except ImportError:
         return None
     return torch.version.cuda
 
 
-def nvcc_cuda_version(nvcc_path: str | None, env: dict[str, str]) -> tuple[str | None, str | None]:
-    if nvcc_path is None:
-        return None, "nvcc was not found in CUDA_HOME, CUDA_PATH, or PATH"
-    try:
-        completed = subprocess.run([nvcc_path, "--version"], check=True, capture_output=True,
-                                   env=env, text=True, timeout=10)
-    except FileNotFoundError:
-        return None, f"nvcc was not found at {nvcc_path}"
-    except subprocess.TimeoutExpired:
-        return None, f"{nvcc_path} --version timed out"
-    except subprocess.CalledProcessError as exc:
-        output = (exc.stdout or exc.stderr or "").strip()
-        return None, f"{nvcc_path} --version failed" + (f": {output}" if output else "")
-    version = parse_nvcc_release(f"{completed.stdout}\n{completed.stderr}")
-    if version is None:
-        return None, f"could not parse CUDA release from {nvcc_path} --version"
-    return version, None
-
-
-def parse_nvcc_release(output: str) -> str | None:
-    match = re.search(r"release\s+(\d+\.\d+)", output)
-    return match.group(1) if match else None
-
-
-def _major_minor(version: str | None) -> tuple[int, int] | None:
-    if version is None:
-        return None
-    match = re.match(r"^\s*(\d+)\.(\d+)", version)
-    return (int(match.group(1)), int(match.group(2))) if match else None
-
-
-def cuda_build_compatibility(torch_cuda: str | None, nvcc_cuda: str | None) -> tuple[str, str | None]:
-    """Torch-extension rule (same classes as the reference): exact, minor_mismatch, major_mismatch."""
-    if torch_cuda is None:
-        return "missing_torch_cuda", "torch.version.cuda is unavailable"
-    if nvcc_cuda is None:
-        return "missing_nvcc", "nvcc CUDA version is unavailable"
-    tv, nv = _major_minor(torch_cuda), _major_minor(nvcc_cuda)
-    if tv is None:
-        return "unparseable_torch_cuda", f"could not parse torch CUDA version {torch_cuda!r}"
-    if nv is None:
-        return "unparseable_nvcc_cuda", f"could not parse nvcc CUDA version {nvcc_cuda!r}"
+def torch_extension_compatibility(torch_cuda: str | None, nvcc_cuda: str | None) -> tuple[str, str | None]:
+    """Whether a torch C++/CUDA extension builds with this nvcc: "exact", "minor_mismatch"
+    (builds, may warn), "major_mismatch" (fails), or "unknown" with the reason."""
+    tv, nv = version_tuple(torch_cuda), version_tuple(nvcc_cuda)
+    if tv is None or nv is None:
+        return "unknown", f"torch CUDA {torch_cuda!r}, nvcc CUDA {nvcc_cuda!r}"
     if tv == nv:
         return "exact", None
-    if tv[0] == nv[0]:
-        return ("minor_mismatch", "PyTorch extension builds may warn: "
-                f"nvcc reports CUDA {nvcc_cuda} but torch was compiled with CUDA {torch_cuda}")
-    return ("major_mismatch", "PyTorch extension builds will fail: "
-            f"nvcc reports CUDA {nvcc_cuda} but torch was compiled with CUDA {torch_cuda}")
+    note = f"nvcc CUDA {nvcc_cuda} vs torch CUDA {torch_cuda}"
+    return ("minor_mismatch", note) if tv[0] == nv[0] else ("major_mismatch", note)
 
 
 def library_build_compatibility(driver_cuda: str | None, nvcc_cuda: str | None) -> tuple[str, str | None]:
     """The C-ABI library links cudart statically: the driver must support nvcc's CUDA."""
-    dv, nv = _major_minor(driver_cuda), _major_minor(nvcc_cuda)
+    dv, nv = version_tuple(driver_cuda), version_tuple(nvcc_cuda)
     if dv is None or nv is None:
         return "unknown", f"driver CUDA {driver_cuda!r}, nvcc CUDA {nvcc_cuda!r}"
     if dv >= nv:
@@ -163,11 +164,11 @@ def require_b200(device_index: int = 0) -> dict[str, Any]:
 def environment_report(env: dict[str, str] | None = None) -> dict[str, Any]:
     env = dict(os.environ if env is None else env)
     prepare_torch_extension_env(env)
-    nvcc = nvcc_path_from_env(env)
-    nvcc_cuda, nvcc_error = nvcc_cuda_version(nvcc, env)
+    probe = probe_nvcc(env)
+    nvcc, nvcc_cuda, nvcc_error = probe.path, probe.release, probe.error
     torch_cuda = torch_cuda_version()
     driver = driver_cuda_version()
-    ext_status, ext_note = cuda_build_compatibility(torch_cuda, nvcc_cuda)
+    ext_status, ext_note = torch_extension_compatibility(torch_cuda, nvcc_cuda)
     lib_status, lib_note = library_build_compatibility(driver, nvcc_cuda)
     return {
         "target": {"name": ACTIVE_TARGET.name, "sm": ACTIVE_TARGET.sm, "gencode": ACTIVE_TARGET.nvcc_gencode},

@@ -92,6 +92,19 @@ __global__ void watchdog_selftest_kernel(int* status, unsigned long long limit_n
   __syncthreads();
 }
 
+// Evaluates the softmax's FMA-pipe exp2 (exp2_poly_x2) elementwise, two inputs per
+// thread exactly as the kernel pairs them, so tests can hold it against CUDA's exp2f.
+__global__ void exp2_poly_eval_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
+  const long long i = 2 * (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  const float x0 = x[i];
+  const float x1 = i + 1 < n ? x[i + 1] : 0.f;
+  float r0, r1;
+  exp2_poly_x2(f2_pack(x0, x1), r0, r1);
+  y[i] = r0;
+  if (i + 1 < n) y[i + 1] = r1;
+}
+
 namespace {
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -363,6 +376,15 @@ extern "C" int avo_b200_watchdog_selftest(int timeout_us, int* status_dev, void*
   return cudaGetLastError() == cudaSuccess ? AVO_B200_OK : AVO_B200_ELAUNCH;
 }
 
+extern "C" int avo_b200_exp2_poly_eval(const float* x, float* y, long long n, void* stream) {
+  if (x == nullptr || y == nullptr || n < 0) return AVO_B200_EINVAL;
+  if (n == 0) return AVO_B200_OK;
+  const long long blocks = ((n + 1) / 2 + 255) / 256;
+  if (blocks > INT_MAX) return AVO_B200_EINVAL;
+  exp2_poly_eval_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);
+  return cudaGetLastError() == cudaSuccess ? AVO_B200_OK : AVO_B200_ELAUNCH;
+}
+
 // ---------------------------------------------------------------- no-allocation split path
 // Scratch of avo_b200_attn_fwd_split_noalloc, held statically on every device the library
 // runs on: a running fp32 accumulator (O and LSE) and one bf16/fp32 partial, each for up to
@@ -427,9 +449,13 @@ extern "C" int avo_b200_attn_fwd_split_noalloc(const void* q, const void* k, con
   if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale)) return AVO_B200_EINVAL;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return AVO_B200_EINVAL;
   if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u) != 0) return AVO_B200_EINVAL;
+  // Size check before any product that could overflow: batch, heads and seq are each
+  // non-negative ints, so batch * heads fits in 64 bits, and the row count is only formed
+  // once it is known to stay within the scratch.
   const long long bh = static_cast<long long>(batch) * heads;
+  if (bh > AVO_B200_NOALLOC_MAX_ROWS || (seq > 0 && bh > AVO_B200_NOALLOC_MAX_ROWS / seq))
+    return AVO_B200_ETOOBIG;
   const long long rows = bh * seq;
-  if (rows > AVO_B200_NOALLOC_MAX_ROWS) return AVO_B200_ETOOBIG;
   if (rows == 0) return AVO_B200_OK;
 
   int rc = prepare_device();

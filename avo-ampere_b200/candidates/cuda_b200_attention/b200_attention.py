@@ -44,6 +44,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     ),
     "avo_b200_acc_to_bf16": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_ll, _c_ll, _vp]),
     "avo_b200_watchdog_selftest": (_c_int, [_c_int, _vp, _vp]),
+    "avo_b200_exp2_poly_eval": (_c_int, [_vp, _vp, _c_ll, _vp]),
     "avo_b200_attn_fwd_split_noalloc": (
         _c_int,
         [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp, _vp],
@@ -326,3 +327,16 @@ def watchdog_selftest(device, timeout_us: int = 20000) -> int:
                                               _stream_handle(word.device))
     _check(code, "avo_b200_watchdog_selftest")
     return int(word.item())
+
+
+def exp2_poly_eval(x):
+    """The kernel's FMA-pipe 2^x on a CUDA fp32 tensor (diagnostic; inputs in [-125, 127])."""
+    torch = _torch()
+    if not x.is_cuda or x.dtype != torch.float32 or not x.is_contiguous():
+        raise RuntimeError("x must be a contiguous CUDA fp32 tensor")
+    y = torch.empty_like(x)
+    lib = load_library()
+    with torch.cuda.device(x.device):
+        code = lib.avo_b200_exp2_poly_eval(x.data_ptr(), y.data_ptr(), x.numel(), _stream_handle(x.device))
+    _check(code, "avo_b200_exp2_poly_eval")
+    return y

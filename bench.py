@@ -10,10 +10,23 @@ scaling, no data-path collective); the timed region is bracketed by a barrier an
 max over ranks is reported.  FLOPs follow the reference accounting
 (avo/benchmark.py:22-27, 54-62): 4*B*H*S^2*D, halved when causal.
 
+Extra keys on the GPU arm's line (same event rules, inputs larger than L2):
+
+* ``target_point`` (1 GPU): B4 H16 S8192 non-causal, the throughput target;
+* ``strong`` (every N): that fixed B4 H16 S8192 problem with its 64 (batch, head) pairs
+  cut into N contiguous shards, one per rank, timed as the max over ranks; rank 0 also
+  times the whole problem alone, which gives the 1-GPU figure the efficiency divides by;
+* ``sdpa_gpu`` (1 GPU): the reference seed's own call, ``F.scaled_dot_product_attention``,
+  on the GPU with the same inputs, for the default dispatch and each SDPA backend;
+* ``sustained`` (1 GPU): the bench workload back to back for >= 2 s, with the median SM
+  clock of that window, against the sustained bf16 peak.
+
 ``--impl reference`` times the reference's own path for this operation on the host
 cores instead: the seed ``candidates/torch_sdpa_seed.py:6-7`` is
 ``F.scaled_dot_product_attention`` (torch 2.11), run here on CPU bf16 tensors (the
 reference scorer itself refuses anything but an sm_86 GPU, avo/benchmark.py:207-215).
+The GPU arm's ``cpu_baseline`` is that same reference arm, run in a child process
+that never touches CUDA, so both report one measurement of one thing.
 """
 
 from __future__ import annotations
@@ -22,6 +35,7 @@ import argparse
 import json
 import os
 import statistics
+import subprocess
 import sys
 import threading
 import time
@@ -216,33 +230,30 @@ def workload_case(name: str):
     return NAMED_CASES[name]
 
 
-def cpu_sdpa_tflops(case, *, min_seconds: float, max_reps: int, heads: int | None = None):
-    """Time the reference seed's call (torch SDPA) on CPU bf16 tensors, one batch
-    entry of the case (``heads`` heads), all host threads.  Returns (tflops, ms, sample)."""
-    import torch
-
-    from avo.benchmark import attention_forward_flops
-    from avo.config import AttentionCase
-    from oracle.attention_oracle import make_inputs, sdpa_reference
-
-    torch.set_num_threads(os.cpu_count() or 1)
-    h = heads or case.num_heads
-    sample = AttentionCase(seq_len=case.seq_len, causal=case.causal, num_heads=h,
-                           total_tokens=case.seq_len, k_scale=case.k_scale)
-    q, k, v = make_inputs(sample.shape, seed=0, k_scale=sample.k_scale)
-    sdpa_reference(q, k, v, sample.causal)  # warm-up
-    times = []
-    start = time.perf_counter()
-    while len(times) < max_reps and (time.perf_counter() - start < min_seconds or len(times) < 1):
-        t0 = time.perf_counter()
-        sdpa_reference(q, k, v, sample.causal)
-        times.append((time.perf_counter() - t0) * 1000.0)
-    ms = statistics.median(times)
-    flops = attention_forward_flops(sample)
-    desc = (f"torch {torch.__version__} F.scaled_dot_product_attention on CPU bf16, "
-            f"B1 H{h} S{case.seq_len} D128 {'causal' if case.causal else 'non-causal'} "
-            f"(one batch entry of the workload), median of {len(times)} after 1 warm-up")
-    return flops / (ms / 1000.0) / 1e12, ms, desc, torch.get_num_threads()
+def cpu_baseline_in_child(args, min_seconds: float = 10.0) -> dict | None:
+    """Run this file's reference arm (``--impl reference``) in a child process with CUDA
+    hidden, so the CPU leg never shares a process with a CUDA context, the clock sampler
+    or pinned buffers, and returns its ``cpu_baseline``."""
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    env["CUDA_VISIBLE_DEVICES"] = ""
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--gpus", "1",
+           "--steps", "20", "--warmup", "2", "--workload", args.workload,
+           "--min-seconds", str(min_seconds)]
+    try:
+        proc = subprocess.run(cmd, capture_output=True, text=True, timeout=300, env=env, cwd=ROOT)
+    except subprocess.TimeoutExpired:
+        return None
+    for line in reversed(proc.stdout.splitlines()):
+        if line.startswith("{"):
+            try:
+                data = json.loads(line)
+            except ValueError:
+                continue
+            cpu = dict(data.get("cpu_baseline") or {})
+            cpu["ms_per_sample"] = data.get("ms_per_step")
+            cpu["how"] = "bench.py --impl reference in a child process with CUDA hidden"
+            return cpu
+    return None
 
 
 def config_dict(case, n_gpus: int, workload: str) -> dict:
@@ -258,6 +269,7 @@ def config_dict(case, n_gpus: int, workload: str) -> dict:
         "causal": case.causal,
         "k_scale": case.k_scale,
         "parallelism": f"head-sharded x{n_gpus} (no collective)",
+        "cpu_sample": f"B1 of B{case.batch_size} (one batch entry, H{case.num_heads} S{case.seq_len}) per CPU step",
         "l2": f"inputs larger than L2: {per_step_bytes / 1e6:.0f} MB q/k/v/o per step per GPU vs 126 MB L2",
     }
 
@@ -288,19 +300,22 @@ def run_reference(args, case) -> int:
     for _ in range(max(0, args.warmup - 1)):
         sdpa_reference(q, k, v, sample.causal)
     times = []
-    for _ in range(args.steps):
+    steps = args.steps
+    if args.min_seconds > 0:  # the GPU arm's baseline leg: about min_seconds of CPU work
+        steps = max(steps, min(2000, int(args.min_seconds / max(first, 1e-6)) + 1))
+    for _ in range(steps):
         t = time.perf_counter()
         sdpa_reference(q, k, v, sample.causal)
         times.append(time.perf_counter() - t)
     total = sum(times)
     flops = attention_forward_flops(sample)
-    value = flops * args.steps / total / 1e12
+    value = flops * steps / total / 1e12
     desc = (f"torch {torch.__version__} F.scaled_dot_product_attention (the reference seed's call) "
             f"on CPU bf16, B1 H{heads} S{case.seq_len} D128 per step "
-            f"(one batch entry of the per-GPU workload); time.perf_counter")
+            f"(one batch entry of the per-GPU workload), {steps} steps; time.perf_counter")
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": total / args.steps * 1000.0, "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": total / steps * 1000.0, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": config_dict(case, args.gpus, args.workload), "impl": "reference",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
@@ -309,6 +324,140 @@ def run_reference(args, case) -> int:
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def time_launches(fn, reps: int, stream) -> float:
+    """Milliseconds per call of ``fn`` over ``reps`` back-to-back calls, CUDA events on
+    ``stream`` with a synchronize on both sides."""
+    import torch
+
+    torch.cuda.synchronize(stream.device)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(reps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize(stream.device)
+    return start.elapsed_time(end) / reps
+
+
+def strong_record(args, lib, device, stream, dist, rank: int, world: int, peak: float) -> dict:
+    """B4 H16 S8192 non-causal (64 independent (batch, head) pairs) split over the ranks:
+    rank r computes pairs [64 r / N, 64 (r + 1) / N).  Every rank draws only its shard
+    (seed + rank); the time is the max over ranks.  Rank 0 then times the whole problem
+    alone (1-GPU baseline of the same run) while the others wait at the barrier."""
+    import torch
+
+    from avo.benchmark import attention_forward_flops, host_inputs
+    from avo.config import NAMED_CASES, AttentionCase
+
+    tcase = NAMED_CASES["b4_h16_s8192_noncausal"]
+    pairs = tcase.batch_size * tcase.num_heads
+    lo, hi = pairs * rank // world, pairs * (rank + 1) // world
+    shard = AttentionCase(seq_len=tcase.seq_len, causal=False, num_heads=hi - lo,
+                          total_tokens=tcase.seq_len)  # B1 x (hi - lo) heads
+    reps = max(5, min(args.steps, 30))
+    tq, tk, tv = (t.to(device) for t in host_inputs(shard, seed=args.seed + rank))
+    to = torch.empty_like(tq)
+
+    def run_shard():
+        lib.attention_forward(tq, tk, tv, False, need_lse=False, out=to)
+
+    for _ in range(3):
+        run_shard()
+    lib.check_status(device)
+    barrier_sync(dist, device)
+    ms_local = time_launches(run_shard, reps, stream)
+    lib.check_status(device)
+    ms = max_over_ranks(dist, ms_local, device)
+    del tq, tk, tv, to
+    total_flops = attention_forward_flops(tcase)
+    record = {"workload": "B4 H16 S8192 D128 non-causal", "ms": ms,
+              "tflops": total_flops / (ms / 1000.0) / 1e12,
+              "pairs_per_rank": [pairs * (r + 1) // world - pairs * r // world for r in range(world)],
+              "ranks": world}
+    record["tflops_per_gpu"] = record["tflops"] / world
+    if world > 1:
+        one_ms = 0.0
+        if rank == 0:
+            fq, fk, fv = (t.to(device) for t in host_inputs(tcase, seed=args.seed))
+            fo = torch.empty_like(fq)
+
+            def run_full():
+                lib.attention_forward(fq, fk, fv, False, need_lse=False, out=fo)
+
+            for _ in range(3):
+                run_full()
+            one_ms = time_launches(run_full, reps, stream)
+            lib.check_status(device)
+            del fq, fk, fv, fo
+        barrier_sync(dist, device)
+        one_ms = max_over_ranks(dist, one_ms, device)
+        one_tflops = total_flops / (one_ms / 1000.0) / 1e12
+        record["one_gpu_ms"] = one_ms
+        record["one_gpu_tflops"] = one_tflops
+        record["efficiency"] = record["tflops_per_gpu"] / one_tflops
+    record["frac_of_measured_peak_per_gpu"] = record["tflops_per_gpu"] / peak
+    return record
+
+
+def sdpa_gpu_record(args, device, stream, case, q, k, v) -> dict:
+    """The reference seed's call (F.scaled_dot_product_attention) on the GPU, same inputs
+    and event rules: torch's default dispatch and each SDPA backend forced in turn."""
+    import torch
+    import torch.nn.functional as F
+
+    from avo.benchmark import attention_forward_flops
+
+    flops = attention_forward_flops(case)
+    reps = max(5, min(args.steps, 30))
+    record: dict = {"workload": f"B{case.batch_size} H{case.num_heads} S{case.seq_len} D128 "
+                                f"{'causal' if case.causal else 'non-causal'}"}
+
+    def timed():
+        def call():
+            F.scaled_dot_product_attention(q, k, v, is_causal=case.causal)
+        for _ in range(3):
+            call()
+        ms = time_launches(call, reps, stream)
+        return {"ms": ms, "tflops": flops / (ms / 1000.0) / 1e12}
+
+    try:
+        record["default"] = timed()
+    except Exception as exc:  # record, do not fail the bench line
+        record["default"] = {"error": f"{type(exc).__name__}: {exc}"[:200]}
+    try:
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+    except ImportError:
+        return record
+    for name in ("CUDNN_ATTENTION", "FLASH_ATTENTION", "EFFICIENT_ATTENTION"):
+        backend = getattr(SDPBackend, name, None)
+        if backend is None:
+            continue
+        try:
+            with sdpa_kernel(backend):
+                record[name.lower()] = timed()
+        except Exception as exc:
+            record[name.lower()] = {"error": f"{type(exc).__name__}: {exc}"[:200]}
+    best = [r["tflops"] for r in record.values() if isinstance(r, dict) and "tflops" in r]
+    record["best_tflops"] = max(best) if best else None
+    return record
+
+
+def sustained_record(step, device, stream, flops: float, lib, sustained_peak: float | None,
+                     seconds: float = 2.5) -> dict:
+    """The bench step back to back for about ``seconds``, clocks sampled throughout."""
+    probe = time_launches(step, 5, stream)
+    reps = max(10, int(seconds * 1000.0 / max(probe, 1e-3)))
+    sampler = ClockSampler(device.index, period_s=0.01)
+    with sampler:
+        ms = time_launches(step, reps, stream)
+    lib.check_status(device)
+    tflops = flops / (ms / 1000.0) / 1e12
+    return {"seconds": ms * reps / 1000.0, "launches": reps, "ms": ms, "tflops": tflops,
+            "frac_of_measured_sustained_peak": (tflops / sustained_peak) if sustained_peak else None,
+            "clocks": sampler.summary()}
 
 
 def run_b200(args, case) -> int:
@@ -415,37 +564,21 @@ def run_b200(args, case) -> int:
         del pq, pk, pv, po, bufs
 
     extra = {}
+    peak, sustained_peak, _ = measured_peaks()
+    if not args.skip_extra:
+        # Strong scaling of the target point (every N, the same collective steps on every
+        # rank): the fixed B4 H16 S8192 problem, its 64 (batch, head) pairs cut into N
+        # contiguous shards.
+        extra["strong"] = strong_record(args, lib, device, stream, dist, rank, world, peak)
     if world == 1 and not args.skip_extra:
-        # The throughput target point, same timing rules.
-        from avo.config import NAMED_CASES
-
-        tcase = NAMED_CASES["b4_h16_s8192_noncausal"]
-        tq, tk, tv = (t.to(device) for t in host_inputs(tcase, seed=args.seed))
-        to = torch.empty_like(tq)
-        for _ in range(3):
-            lib.attention_forward(tq, tk, tv, False, need_lse=False, out=to)
-        torch.cuda.synchronize(device)
-        s3 = torch.cuda.Event(enable_timing=True)
-        e3 = torch.cuda.Event(enable_timing=True)
-        reps = max(5, min(args.steps, 30))
-        s3.record(stream)
-        for _ in range(reps):
-            lib.attention_forward(tq, tk, tv, False, need_lse=False, out=to)
-        e3.record(stream)
-        torch.cuda.synchronize(device)
-        lib.check_status(device)
-        t_ms = s3.elapsed_time(e3) / reps
-        t_tflops = attention_forward_flops(tcase) / (t_ms / 1000.0) / 1e12
-        peak, _, _ = measured_peaks()
-        extra["target_point"] = {"workload": "B4 H16 S8192 D128 non-causal", "ms": t_ms,
-                                 "tflops": t_tflops, "frac_of_measured_peak": t_tflops / peak}
-        del tq, tk, tv, to
+        extra["target_point"] = {k: extra["strong"][k] for k in ("workload", "ms", "tflops")}
+        extra["target_point"]["frac_of_measured_peak"] = extra["strong"]["tflops"] / peak
+        extra["sdpa_gpu"] = sdpa_gpu_record(args, device, stream, case, q, k, v)
+        extra["sustained"] = sustained_record(step, device, stream, flops, lib, sustained_peak)
 
     cpu = None
     if world == 1 and rank == 0 and not args.skip_cpu:
-        tflops, cpu_ms, desc, threads = cpu_sdpa_tflops(case, min_seconds=10.0, max_reps=20)
-        cpu = {"value": tflops, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": desc, "ms_per_sample": cpu_ms}
+        cpu = cpu_baseline_in_child(args)
 
     if rank == 0:
         peak, sustained, peak_kind = measured_peaks()
@@ -504,6 +637,8 @@ def main(argv=None) -> int:
     parser.add_argument("--skip-e2e", action="store_true")
     parser.add_argument("--skip-cpu", action="store_true")
     parser.add_argument("--skip-extra", action="store_true")
+    parser.add_argument("--min-seconds", type=float, default=0.0,
+                        help="reference arm: run at least this long (the GPU arm's CPU-baseline leg)")
     args = parser.parse_args(argv)
     if args.warmup < 3 and args.impl == "b200":
         parser.error("--warmup must be >= 3")

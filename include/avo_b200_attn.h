@@ -133,6 +133,15 @@ int avo_b200_attn_fwd_split_noalloc(const void* q, const void* k, const void* v,
  */
 int avo_b200_watchdog_selftest(int timeout_us, int* status_dev, void* stream);
 
+/*
+ * Diagnostic (no reference counterpart): y[i] = the softmax's FMA-pipe 2^x[i] for
+ * x[i] in [-125, 127], computed by the same device function the attention kernel uses
+ * for part of its exponentials (degree-3 relative-minimax polynomial after a
+ * Cody-Waite split; relative error < 7.5e-5).  x and y are fp32 device arrays of n
+ * elements.  Exists so tests can compare it with CUDA's exp2f on the device.
+ */
+int avo_b200_exp2_poly_eval(const float* x, float* y, long long n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,7 +1,7 @@
 """Generate golden attention vectors from the reference's own oracle seed.
 
 Imports ``candidates/torch_sdpa_seed.py`` from the reference checkout (path given by
-``--reference``, default /root/reference) and runs its ``attention(q, k, v, causal)``
+the required ``--reference`` flag) and runs its ``attention(q, k, v, causal)``
 on the CPU for small seeded cases:
 
 * ``o_bf16``  - the seed on the bf16 inputs (what the reference scorer compares with);
@@ -11,7 +11,7 @@ Inputs are stored as bf16 bit patterns (uint16), outputs as bf16 bits / float32,
 ``attention_golden.npz`` next to this script, with a JSON manifest of the cases.  The
 reference cannot travel to the GPU machine, so tests use only the stored file.
 
-Usage: ``python tests/golden/make_golden.py [--reference PATH]``
+Usage: ``python tests/golden/make_golden.py --reference PATH``
 """
 
 from __future__ import annotations
@@ -59,7 +59,7 @@ def bf16_bits(t: torch.Tensor) -> np.ndarray:
 
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="root of the reference checkout")
     args = parser.parse_args()
     seed_path = Path(args.reference) / "candidates" / "torch_sdpa_seed.py"
     spec = importlib.util.spec_from_file_location("reference_torch_sdpa_seed", seed_path)

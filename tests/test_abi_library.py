@@ -79,6 +79,11 @@ def test_host_side_argument_checks(b200):
     assert noalloc(fake, fake, fake, fake, None, 1, 1, 16384 + 128, 128, 0, 0.088, 2, None, None) == 6
     assert noalloc(fake, fake, fake, fake, None, 2, 16, 1024, 128, 0, 0.088, 2, None, None) == 6
     assert noalloc(fake, fake, fake, fake, None, 0, 16, 1024, 128, 0, 0.088, 2, None, None) == 0
+    # Dimensions whose row product overflows 64 bits are refused as too large, not wrapped.
+    int_max = 2**31 - 1
+    assert noalloc(fake, fake, fake, fake, None, int_max, int_max, 4, 128, 0, 0.088, 2, None, None) == 6
+    assert noalloc(fake, fake, fake, fake, None, int_max, int_max, int_max, 128, 0, 0.088, 2, None, None) == 6
+    assert noalloc(fake, fake, fake, fake, None, 1, int_max, 2, 128, 0, 0.088, 2, None, None) == 6
     assert "too large" in b200.strerror(6)
 
 
