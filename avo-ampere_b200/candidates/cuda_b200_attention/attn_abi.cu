@@ -208,6 +208,17 @@ int prepare_device(int* sm_count = nullptr) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Whether the current device supports cooperative launches (all CTAs resident at once).
+bool cooperative_ok() {
+  int dev = -1, coop = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  return coop != 0;
+}
+
 // [heads, rows, 128] bf16 view with `head_stride` elements between heads; TMA box of
 // 64 columns x 128 rows x 1 head, 128-byte swizzle.
 int encode_rows(CUtensorMap* map, const void* base, int rows, int heads, long long head_stride) {
@@ -224,10 +235,35 @@ int encode_rows(CUtensorMap* map, const void* base, int rows, int heads, long lo
   return r == CUDA_SUCCESS ? AVO_B200_OK : AVO_B200_ETENSORMAP;
 }
 
+// Scratch for split pieces inside a caller's workspace (zero-filled once by the caller; a
+// launch that completes leaves every flag at 0 again): flags, then per slot m/l, then O.
+struct SplitScratch {
+  int* flags;
+  float* ml;
+  float* o;
+};
+constexpr size_t kFlagBytesPerCta = 2 * kQTiles * sizeof(int);
+constexpr size_t kMlBytesPerCta = 2 * kQTiles * kSlotMl * sizeof(float);
+constexpr size_t kOBytesPerCta = 2 * kQTiles * static_cast<size_t>(kSlotO) * sizeof(float);
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+size_t workspace_bytes_for(int sms) {
+  const size_t n = static_cast<size_t>(sms);
+  return round_up(n * kFlagBytesPerCta, 256) + round_up(n * kMlBytesPerCta, 256) + n * kOBytesPerCta;
+}
+SplitScratch carve_workspace(void* ws, int sms) {
+  const size_t n = static_cast<size_t>(sms);
+  char* base = static_cast<char*>(ws);
+  SplitScratch s;
+  s.flags = reinterpret_cast<int*>(base);
+  s.ml = reinterpret_cast<float*>(base + round_up(n * kFlagBytesPerCta, 256));
+  s.o = reinterpret_cast<float*>(base + round_up(n * kFlagBytesPerCta, 256) + round_up(n * kMlBytesPerCta, 256));
+  return s;
+}
+
 int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int num_bh,
                int seq_q, int seq_kv, int head_dim, long long q_hs, long long kv_hs, long long o_hs,
                long long lse_hs, int causal, float scale, long long q_pos0, long long kv_pos0,
-               int* status, void* stream) {
+               int* status, void* stream, void* workspace = nullptr, size_t workspace_bytes = 0) {
   if (q == nullptr || k == nullptr || v == nullptr || o == nullptr) return AVO_B200_EINVAL;
   if (head_dim != kHeadDim || num_bh < 0 || seq_q < 0 || seq_kv < 0) return AVO_B200_EINVAL;
   if (!(scale > 0.f) || !std::isfinite(scale)) return AVO_B200_EINVAL;
@@ -244,12 +280,19 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   int rc = prepare_device(&sm_count);
   if (rc != AVO_B200_OK) return rc;
 
-  // Persistent grid: one CTA per multiprocessor (the kernel's shared memory admits one),
-  // each looping over 256-row query blocks.
+  // Persistent grid: at most one CTA per multiprocessor (the kernel's shared memory admits
+  // one), each walking its units of 256-row query blocks (schedule.cuh).
   const int num_q_blocks = (seq_q + kRowsPerCta - 1) / kRowsPerCta;
   const long long items = static_cast<long long>(num_bh) * num_q_blocks;
   if (items > INT_MAX) return AVO_B200_EINVAL;
-  const int grid = static_cast<int>(std::min<long long>(items, sm_count));
+  if (static_cast<long long>(num_bh) * ((seq_kv + kBlockN - 1) / kBlockN) * num_q_blocks > INT_MAX)
+    return AVO_B200_EINVAL;
+  const bool split_ok = workspace != nullptr && cooperative_ok();
+  if (workspace != nullptr && workspace_bytes < workspace_bytes_for(sm_count)) return AVO_B200_EINVAL;
+  if (workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return AVO_B200_EINVAL;
+  const sched::Plan plan =
+      sched::make_plan(num_bh, seq_q, seq_kv, causal, q_pos0, kv_pos0, sm_count, split_ok);
+  const int grid = plan.grid;
 
   alignas(64) CUtensorMap tm_q, tm_k, tm_v;
   const int kv_rows = seq_kv > 0 ? seq_kv : 1;  // never read when seq_kv == 0
@@ -257,7 +300,14 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   if ((rc = encode_rows(&tm_k, k, kv_rows, num_bh, kv_hs)) != AVO_B200_OK) return rc;
   if ((rc = encode_rows(&tm_v, v, kv_rows, num_bh, kv_hs)) != AVO_B200_OK) return rc;
 
-  AttnParams p;
+  AttnParams p{};
+  p.plan = plan;
+  if (plan.mode != sched::kWaves) {
+    const SplitScratch sc = carve_workspace(workspace, sm_count);
+    p.part_flag = sc.flags;
+    p.part_ml = sc.ml;
+    p.part_o = sc.o;
+  }
   p.lse = lse;
   p.o = o;
   p.o_head_stride = o_hs;
@@ -271,12 +321,23 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   p.seq_q = seq_q;
   p.seq_kv = seq_kv;
   p.num_bh = num_bh;
-  p.num_q_blocks = num_q_blocks;
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale * 1.4426950408889634f;
 
-  attn_fwd_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
-      tm_q, tm_k, tm_v, p);
+  if (plan.mode == sched::kWaves) {
+    attn_fwd_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
+        tm_q, tm_k, tm_v, p);
+  } else {
+    // Split pieces: a CTA that merges an item waits for its neighbours' continuation
+    // pieces, so every CTA must be resident at once; a cooperative launch guarantees it
+    // (or fails to launch).
+    void* args[] = {&tm_q, &tm_k, &tm_v, &p};
+    if (cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(attn_fwd_kernel), dim3(grid), dim3(kThreads),
+                                    args, kSmemBytes, static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return AVO_B200_ELAUNCH;
+    }
+  }
   if (cudaGetLastError() != cudaSuccess) return AVO_B200_ELAUNCH;
   return AVO_B200_OK;
 }
@@ -311,6 +372,55 @@ extern "C" int avo_b200_attn_fwd(const void* q, const void* k, const void* v, vo
   const long long hs = static_cast<long long>(seq) * kHeadDim;
   return launch_fwd(q, k, v, o, lse, static_cast<int>(bh), seq, seq, head_dim, hs, hs, hs, seq, causal,
                     softmax_scale, 0, 0, status_dev, stream);
+}
+
+extern "C" int avo_b200_attn_workspace_size(size_t* bytes) {
+  if (bytes == nullptr) return AVO_B200_EINVAL;
+  int sm_count = 0;
+  const int rc = prepare_device(&sm_count);
+  if (rc != AVO_B200_OK) return rc;
+  *bytes = workspace_bytes_for(sm_count);
+  return AVO_B200_OK;
+}
+
+extern "C" int avo_b200_attn_fwd_ws(const void* q, const void* k, const void* v, void* o, float* lse, int batch,
+                                    int heads, int seq, int head_dim, int causal, float softmax_scale,
+                                    void* workspace, size_t workspace_bytes, int* status_dev, void* stream) {
+  if (batch < 0 || heads < 0 || seq < 0) return AVO_B200_EINVAL;
+  const long long bh = static_cast<long long>(batch) * heads;
+  if (bh > INT_MAX) return AVO_B200_EINVAL;
+  const long long hs = static_cast<long long>(seq) * kHeadDim;
+  return launch_fwd(q, k, v, o, lse, static_cast<int>(bh), seq, seq, head_dim, hs, hs, hs, seq, causal,
+                    softmax_scale, 0, 0, status_dev, stream, workspace, workspace_bytes);
+}
+
+extern "C" int avo_b200_schedule_units(int num_bh, int seq_q, int seq_kv, int causal, long long q_pos0,
+                                       long long kv_pos0, int sm_count, int split, int* plan_out,
+                                       int* units, int max_units, int* counts) {
+  if (num_bh < 0 || seq_q < 0 || seq_kv < 0 || sm_count <= 0 || plan_out == nullptr || max_units < 0)
+    return AVO_B200_EINVAL;
+  const sched::Plan plan =
+      sched::make_plan(num_bh, seq_q, seq_kv, causal, q_pos0, kv_pos0, sm_count, split != 0);
+  plan_out[0] = plan.mode;
+  plan_out[1] = plan.grid;
+  plan_out[2] = plan.group_pairs;
+  plan_out[3] = plan.wave_items;
+  if (units == nullptr || counts == nullptr) return AVO_B200_OK;
+  for (int c = 0; c < plan.grid; ++c) {
+    sched::Walker walk(plan, c);
+    sched::Unit u;
+    int n = 0;
+    while (walk.next(u)) {
+      if (n < max_units) {
+        int* e = units + (static_cast<long long>(c) * max_units + n) * 8;
+        e[0] = u.bh; e[1] = u.q0; e[2] = u.t0; e[3] = u.t1; e[4] = u.kind; e[5] = u.seg;
+        e[6] = u.cont_lo; e[7] = u.cont_hi;
+      }
+      ++n;
+    }
+    counts[c] = n;
+  }
+  return AVO_B200_OK;
 }
 
 extern "C" int avo_b200_attn_fwd_block(const void* q, const void* k, const void* v, void* o, float* lse,

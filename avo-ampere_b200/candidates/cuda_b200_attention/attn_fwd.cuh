@@ -37,6 +37,7 @@
 
 #include <type_traits>
 
+#include "schedule.cuh"
 #include "sm100_ptx.cuh"
 
 // Optional per-tile timeline hooks (role, tile, event) for development builds; they
@@ -65,6 +66,7 @@ constexpr int kWaitWarp = 10;
 constexpr uint32_t kBarMmaHandoff = 3;
 constexpr uint32_t kBarPHalf = 4;
 constexpr uint32_t kBarOFree = 8;
+constexpr uint32_t kBarSlot = 10;              // 10 + tile: the tile's 4 softmax warps (split pieces)
 constexpr uint32_t kPHalfThreads = 128 + 32;
 constexpr int kThreads = 384;                  // 3 warpgroups: softmax 0, softmax 1, load/MMA/waiter
 // Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512), the
@@ -109,6 +111,7 @@ constexpr int kSmemBytes = kSmemUsed + 1024;  // slack for the manual 1024-byte 
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 struct AttnParams {
+  sched::Plan plan;             // work units of every CTA (schedule.cuh)
   float* lse;                   // [num_bh, lse_head_stride] natural-log LSE, or null
   int* status;                  // device status word, or null
   long long lse_head_stride;    // elements between consecutive heads of lse
@@ -118,14 +121,27 @@ struct AttnParams {
   int seq_q;
   int seq_kv;
   int num_bh;
-  int num_q_blocks;             // ceil(seq_q / 256)
   void* o;                      // bf16 output rows, [num_bh, o_head_stride]
   int o_sector_aligned;         // o and o_head_stride * 2 bytes are multiples of 32
   long long o_head_stride;      // elements between consecutive heads of o
   int causal;                   // key position > query position is masked
   float scale_log2;             // softmax_scale * log2(e)
   int test_skip_load;           // test hook: K/V copy index the producer never issues, or -1
+  // Split pieces (stream-K plans only; null otherwise).  Per CTA, per segment parity, per
+  // Q tile: one slot of 128 rows: unnormalised O (fp32, 16 pieces of 8 values per row,
+  // piece-major so that a warp's stores are contiguous), the row max m and sum l, and a
+  // flag (1 = the slot holds a continuation piece not yet merged, 0 = free).
+  float* part_o;
+  float* part_ml;
+  int* part_flag;
 };
+
+// Scratch of one slot (CTA, segment parity, Q tile).
+constexpr int kSlotO = 16 * kBlockM * 8;  // floats
+constexpr int kSlotMl = 2 * kBlockM;       // floats
+__host__ __device__ constexpr long long slot_index(int cta, int parity, int tile) {
+  return (static_cast<long long>(cta) * 2 + parity) * kQTiles + tile;
+}
 
 struct Watch {
   volatile int* abort;
@@ -264,49 +280,40 @@ __device__ __forceinline__ float exp_half_max(const uint32_t (&s)[4][32], uint64
   return fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
 }
 
-// Work item w (one CTA-sized block of 256 query rows of one head).  Causal grids run the
-// longest query blocks first.  n_tiles = KV tiles the block sees (0 if none).
-struct Item {
-  int bh, q0, n_tiles;
-};
-__device__ __forceinline__ Item item_at(int w, const AttnParams& p) {
-  int bh, qb;
-  if (p.causal) {
-    qb = p.num_q_blocks - 1 - w / p.num_bh;
-    bh = w % p.num_bh;
-  } else {
-    bh = w / p.num_q_blocks;
-    qb = w % p.num_q_blocks;
+// Flag of a split-piece slot: poll with acquire semantics until it holds `want`, bounded
+// by the watchdog.  One lane polls; the warp then proceeds together.
+__device__ __forceinline__ bool wait_flag(const int* flag, int want, const Watch& w) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) {
+    if (ld_acquire_gpu(flag) != want) {
+      const uint64_t t0 = global_timer_ns();
+      while (true) {
+        if (ld_acquire_gpu(flag) == want) break;
+        if (*w.abort) { ok = false; break; }
+        if (global_timer_ns() - t0 > w.limit_ns) {
+          *w.abort = 1;
+          if (w.status != nullptr) atomicOr(w.status, kStatusWatchdog);
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
   }
-  const int q0 = qb * kRowsPerCta;
-  const int n_kv_total = (p.seq_kv + kBlockN - 1) / kBlockN;
-  int n_tiles = n_kv_total;
-  if (p.causal) {
-    const long long q_last = p.q_pos0 + min(q0 + kRowsPerCta, p.seq_q) - 1;
-    const long long lim = q_last - p.kv_pos0;  // largest local key index any row may see
-    n_tiles = lim < 0 ? 0 : static_cast<int>(min(static_cast<long long>(n_kv_total), lim / kBlockN + 1));
-  }
-  return Item{bh, q0, n_tiles};
+  const bool all = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  __threadfence();  // every lane's later reads of the slot are ordered after lane 0's acquire
+  return all;
 }
 
-// Item of this CTA in wave r (gridDim.x items per wave): the CTAs walk the waves in
-// alternating directions, which balances the causal grid's decreasing item lengths
-// across CTAs as well as greedy list scheduling does.  May be >= the item count in
-// the last wave.
-__device__ __forceinline__ int wave_item(int r) {
-  return r * static_cast<int>(gridDim.x) +
-         ((r & 1) ? static_cast<int>(gridDim.x - 1 - blockIdx.x) : static_cast<int>(blockIdx.x));
-}
-
-// Persistent: each CTA processes one item per wave (wave_item).  Every role walks the same
+// Persistent: each CTA walks its unit sequence (schedule.cuh).  Every role walks the same
 // sequence and derives all mbarrier phases from running counters (tiles, ring positions,
-// Q loads), so the pipeline flows from one item into the next: the producer loads the
-// next item's Q as soon as the current item's last S MMAs have read Q, and the MMA warp
-// computes the next item's first S tiles while the softmax warpgroups finish the current
-// item's epilogue.
+// Q loads), so the pipeline flows from one unit into the next: the producer loads the
+// next unit's Q as soon as the current unit's last S MMAs have read Q, and the MMA warp
+// computes the next unit's first S tiles while the softmax warpgroups finish the current
+// unit's epilogue.
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ AttnParams p) {
   extern __shared__ uint8_t smem_dyn[];
   const uint32_t raw = smem_addr(smem_dyn);
   uint8_t* smem = smem_dyn + ((1024u - (raw & 1023u)) & 1023u);
@@ -318,7 +325,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemAbort);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemTmemSlot);
   const Watch watch{abort_flag, p.status, p.watchdog_ns};
-  const int n_items = p.num_bh * p.num_q_blocks;
 
   if (threadIdx.x == 0) {
     mbar_init(bar(BAR_Q), 1);
@@ -363,31 +369,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tO = tmem + lane_off + 2 * kBlockN + i * kHeadDim;
     const float scale = p.scale_log2;
     bool ok = true;
-    // rg = 4 * wave + 2 * parity of the earlier items with work (the O_DONE phase) +
-    // parity of their tiles (the S_FULL phase base), one register for all three.
-    for (int rg = 0; (rg >> 2) * static_cast<int>(gridDim.x) < n_items; rg += 4) {
-      const int r = rg >> 2;
-      const int w = wave_item(r);
-      if (w >= n_items) continue;
-      const Item it = item_at(w, p);
-      const int n_tiles = it.n_tiles;
+    // ph bit 0: parity of the tiles of earlier units (the S_FULL phase base); bit 1: parity
+    // of the earlier units with work (the O_DONE phase).
+    uint32_t ph = 0;
+    sched::Walker walk(p.plan, static_cast<int>(blockIdx.x));
+    sched::Unit u;
+    while (walk.next(u)) {
+      const int n_tiles = u.t1 - u.t0;
       // Visible keys as local key counts in [0, seq_kv]: this row sees keys [0, row_keys);
-      // every row of this warp sees at least the first warp_keys.
+      // every row of this warp sees at least the first warp_keys.  Key counts are relative
+      // to the unit's first tile.
       int row_keys = p.seq_kv, warp_keys = p.seq_kv;
       if (p.causal) {
-        const long long rk = p.q_pos0 + it.q0 + i * kBlockM + t - p.kv_pos0 + 1;
-        const long long wk = p.q_pos0 + it.q0 + i * kBlockM + wq * 32 - p.kv_pos0 + 1;
+        const long long rk = p.q_pos0 + u.q0 + i * kBlockM + t - p.kv_pos0 + 1;
+        const long long wk = p.q_pos0 + u.q0 + i * kBlockM + wq * 32 - p.kv_pos0 + 1;
         row_keys = static_cast<int>(max(0LL, min(static_cast<long long>(p.seq_kv), rk)));
         warp_keys = static_cast<int>(max(0LL, min(static_cast<long long>(p.seq_kv), wk)));
       }
+      row_keys -= u.t0 * kBlockN;
+      warp_keys -= u.t0 * kBlockN;
 
       float m = -CUDART_INF_F;  // running max, log2 units (already scaled)
       float l = 0.f;            // running sum of exp2(s*scale - m)
 
       int j = 0;
       for (; ok && j < n_tiles; ++j) {
-        const int g = rg ^ j;  // bit 0: parity of this tile's index over the CTA's items
-        ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_S_FULL + i), g & 1, watch));
+        ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_S_FULL + i), (ph ^ j) & 1u, watch));
         if (!ok) break;
         AVO_TRACE_HOOK(i, j, 0);
         tc_fence_after();
@@ -505,51 +512,108 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       if (ok && n_tiles > 0) {
-        ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (rg >> 1) & 1, watch));
+        ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (ph >> 1) & 1u, watch));
         tc_fence_after();
       }
 
-      // Epilogue: O / l -> bf16 -> this thread's output row, written straight from
-      // registers as 8 whole 32-byte sectors (16-byte stores when o or its head stride is
-      // not 32-byte aligned; rows past seq_q are not written).  The Q buffer is not
-      // used for staging: the next item's Q may already be loading into it.  A row that
-      // never saw a key keeps m = -inf (its l only holds the FMA-path exp2 floor of
-      // masked scores): it gets O = 0 and LSE = -inf.  Once a row sees a key, the first
-      // rescale multiplies O and l by 2^(-inf) = 0, so no floor survives.
-      const bool seen = (m != -CUDART_INF_F) && (l > 0.f);
-      const float inv_l = seen ? 1.f / l : 0.f;
-      // (The item's head and rows are derived again here rather than kept in registers
-      // across the tile loop.)
-      const Item ie = item_at(wave_item(r), p);
-      const int row = ie.q0 + i * kBlockM + t;
+      // Epilogue.  A whole item: O / l -> bf16 -> this thread's output row, written
+      // straight from registers as 8 whole 32-byte sectors (16-byte stores when o or its
+      // head stride is not 32-byte aligned; rows past seq_q are not written).  The Q
+      // buffer is not used for staging: the next unit's Q may already be loading into it.
+      // A row that never saw a key keeps m = -inf (its l only holds the FMA-path exp2
+      // floor of masked scores): it gets O = 0 and LSE = -inf.  Once a row sees a key, the
+      // first rescale multiplies O and l by 2^(-inf) = 0, so no floor survives.
+      // A continuation piece of a split item writes its unnormalised O, m and l to this
+      // CTA's slot instead; the item's first piece merges those of CTAs cont_lo..cont_hi
+      // (m = max over pieces, O and l rescaled by 2^(m_piece - m)) before normalising.
+      const bool have = ok && n_tiles > 0;
+      const int parity = u.seg & 1;
+      const int row = u.q0 + i * kBlockM + t;
       const bool write = row < p.seq_q && *abort_flag == 0;
+      float m_fin = (have && l > 0.f) ? m : -CUDART_INF_F;
+      float l_fin = m_fin == -CUDART_INF_F ? 0.f : l;
+      float f_own = 1.f;
+      if (u.kind == sched::kFirst) {
+        for (int c = u.cont_lo; c <= u.cont_hi; ++c) {
+          const long long sl = slot_index(c, parity, i);
+          ok = wait_flag(p.part_flag + sl, 1, watch) && ok;
+          if (ok) m_fin = fmaxf(m_fin, __ldcg(p.part_ml + sl * kSlotMl + t));
+        }
+        f_own = (m_fin == -CUDART_INF_F || !(l_fin > 0.f)) ? 0.f : ex2_approx(m - m_fin);
+        l_fin *= f_own;
+        if (ok) {
+          for (int c = u.cont_lo; c <= u.cont_hi; ++c) {
+            const long long sl = slot_index(c, parity, i);
+            const float mc = __ldcg(p.part_ml + sl * kSlotMl + t);
+            if (mc != -CUDART_INF_F) l_fin += __ldcg(p.part_ml + sl * kSlotMl + kBlockM + t) * ex2_approx(mc - m_fin);
+          }
+        }
+      } else if (u.kind == sched::kCont) {
+        ok = wait_flag(p.part_flag + slot_index(blockIdx.x, parity, i), 0, watch) && ok;
+      }
+      const bool seen = (m_fin != -CUDART_INF_F) && (l_fin > 0.f);
+      const float inv_l = seen ? 1.f / l_fin : 0.f;
       __nv_bfloat16* orow =
-          static_cast<__nv_bfloat16*>(p.o) + (static_cast<long long>(ie.bh) * p.o_head_stride +
+          static_cast<__nv_bfloat16*>(p.o) + (static_cast<long long>(u.bh) * p.o_head_stride +
                                               static_cast<long long>(row) * kHeadDim);
-#pragma unroll
+      float* const cont_o = p.part_o + slot_index(blockIdx.x, parity, i) * kSlotO;
+#pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
-        if (ok && n_tiles > 0) {
+        if (have) {
           tmem_ld32(tO + c * 32, o);
           tmem_wait_ld(o);
         } else {
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = 0u;
         }
+        if (u.kind == sched::kCont) {
+          if (ok && *abort_flag == 0) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              st_global_v8(cont_o + ((c * 4 + q) * kBlockM + t) * 8, o[8 * q], o[8 * q + 1], o[8 * q + 2],
+                           o[8 * q + 3], o[8 * q + 4], o[8 * q + 5], o[8 * q + 6], o[8 * q + 7]);
+          }
+          continue;
+        }
+        if (u.kind == sched::kFirst && ok) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = f2u(u2f(o[e]) * f_own);
+          for (int cc = u.cont_lo; cc <= u.cont_hi; ++cc) {
+            const long long sl = slot_index(cc, parity, i);
+            const float mc = __ldcg(p.part_ml + sl * kSlotMl + t);
+            if (mc == -CUDART_INF_F) continue;
+            const float fc = ex2_approx(mc - m_fin);
+            const float4* src = reinterpret_cast<const float4*>(p.part_o + sl * kSlotO);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float4 a = __ldcg(src + ((c * 4 + q) * kBlockM + t) * 2);
+              const float4 b = __ldcg(src + ((c * 4 + q) * kBlockM + t) * 2 + 1);
+              o[8 * q + 0] = f2u(fmaf(a.x, fc, u2f(o[8 * q + 0])));
+              o[8 * q + 1] = f2u(fmaf(a.y, fc, u2f(o[8 * q + 1])));
+              o[8 * q + 2] = f2u(fmaf(a.z, fc, u2f(o[8 * q + 2])));
+              o[8 * q + 3] = f2u(fmaf(a.w, fc, u2f(o[8 * q + 3])));
+              o[8 * q + 4] = f2u(fmaf(b.x, fc, u2f(o[8 * q + 4])));
+              o[8 * q + 5] = f2u(fmaf(b.y, fc, u2f(o[8 * q + 5])));
+              o[8 * q + 6] = f2u(fmaf(b.z, fc, u2f(o[8 * q + 6])));
+              o[8 * q + 7] = f2u(fmaf(b.w, fc, u2f(o[8 * q + 7])));
+            }
+          }
+        }
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) w[e] = pack_bf16x2(u2f(o[2 * e]) * inv_l, u2f(o[2 * e + 1]) * inv_l);
-        if (write && p.o_sector_aligned) {
+        if (write && ok && p.o_sector_aligned) {
           st_global_v8(orow + c * 32, w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7]);
           st_global_v8(orow + c * 32 + 16, w[8], w[9], w[10], w[11], w[12], w[13], w[14], w[15]);
-        } else if (write) {
+        } else if (write && ok) {
           uint4* o16 = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
           for (int q = 0; q < 4; ++q) o16[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
         }
       }
       if (n_tiles > 0) {
-        // O_i may now be overwritten by the next item's first PV.
+        // O_i may now be overwritten by the next unit's first PV.
         tc_fence_before();
         __syncwarp();
         if (ok) {
@@ -558,11 +622,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           named_bar_sync(kBarOFree + i, kPHalfThreads);
         }
       }
-      if (p.lse != nullptr && write) {
-        const float lse = seen ? (m + log2f(l)) * 0.69314718055994531f : -CUDART_INF_F;
-        p.lse[static_cast<long long>(ie.bh) * p.lse_head_stride + row] = lse;
+      if (u.kind == sched::kCont) {
+        // Row max and sum, then publish the slot once all 128 rows are in it.
+        float* ml = p.part_ml + slot_index(blockIdx.x, parity, i) * kSlotMl;
+        if (ok && *abort_flag == 0) {
+          ml[t] = m_fin;
+          ml[kBlockM + t] = l_fin;
+        }
+        __threadfence();  // this thread's slot writes are visible GPU-wide before the flag
+        named_bar_sync(kBarSlot + i, 128);
+        if (t == 0 && ok && *abort_flag == 0) st_release_gpu(p.part_flag + slot_index(blockIdx.x, parity, i), 1);
+      } else if (u.kind == sched::kFirst) {
+        // Every row of this tile has read the continuation pieces: free their slots.
+        named_bar_sync(kBarSlot + i, 128);
+        if (t == 0 && ok) {
+          __threadfence();
+          for (int c = u.cont_lo; c <= u.cont_hi; ++c) st_release_gpu(p.part_flag + slot_index(c, parity, i), 0);
+        }
       }
-      if (n_tiles > 0) rg ^= 2 | (n_tiles & 1);
+      if (p.lse != nullptr && write && ok && u.kind != sched::kCont) {
+        const float lse = seen ? (m_fin + log2f(l_fin)) * 0.69314718055994531f : -CUDART_INF_F;
+        p.lse[static_cast<long long>(u.bh) * p.lse_head_stride + row] = lse;
+      }
+      if (n_tiles > 0) ph ^= 2u | static_cast<uint32_t>(n_tiles & 1);
     }
   } else if (warp == kLoadWarp) {
     regs_decrease<kRegsOther>();
@@ -579,11 +661,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // No separate L2 prefetch of K/V: measured on B200 it cost 1-2 % here (the prefetch
       // operations share the TMA unit with the loads), the CTAs of a head reading the same
       // tiles close together in time already hit L2.
-      for (int r = 0; r * static_cast<int>(gridDim.x) < n_items && !stop; ++r) {
-        const int w = wave_item(r);
-        if (w >= n_items) continue;
-        const Item it = item_at(w, p);
-        if (it.n_tiles == 0) continue;
+      sched::Walker walk(p.plan, static_cast<int>(blockIdx.x));
+      sched::Unit u;
+      while (!stop && walk.next(u)) {
+        const int n_tiles = u.t1 - u.t0;
+        if (n_tiles == 0) continue;
         if (nq > 0) {
           // The previous item's last S MMAs have read Q (committed to Q_EMPTY), and its
           // Q load has landed (as for the K/V slots below: always true unless aborted).
@@ -594,10 +676,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(bar(BAR_Q), kQTiles * kTileBytes);
         for (int i = 0; i < kQTiles; ++i)
           for (int h = 0; h < 2; ++h)
-            tma_load_3d(sQ + i * kTileBytes + h * kHalfBytes, &tm_q, bar(BAR_Q), h * 64, it.q0 + i * kBlockM,
-                        it.bh, pol_q);
+            tma_load_3d(sQ + i * kTileBytes + h * kHalfBytes, &tm_q, bar(BAR_Q), h * 64, u.q0 + i * kBlockM,
+                        u.bh, pol_q);
         ++nq;
-        for (int lt = 0; lt < 2 * it.n_tiles; ++lt, ++tt) {
+        for (int lt = 0; lt < 2 * n_tiles; ++lt, ++tt) {
           const int slot = tt % kStages;
           const int use = tt / kStages;
           if (use > 0) {
@@ -613,10 +695,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           AVO_TRACE_HOOK(3, lt >> 1, lt & 1);
           mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), kTileBytes);
           const CUtensorMap* tm = (lt & 1) ? &tm_v : &tm_k;
-          const int krow = (lt >> 1) * kBlockN;
+          const int krow = (u.t0 + (lt >> 1)) * kBlockN;
           for (int h = 0; h < 2; ++h)
             tma_load_3d(sRing + slot * kTileBytes + h * kHalfBytes, tm, bar(BAR_KV_FULL + slot), h * 64, krow,
-                        it.bh, pol_kv);
+                        u.bh, pol_kv);
           last_copy = (last_copy & ~(3u << (2 * slot))) | ((1u | ((use & 1u) << 1)) << (2 * slot));
         }
       }
@@ -674,11 +756,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // started the ring; the indices are a function of the loop counter alone, which
     // keeps the issue code between barrier and MMA minimal.
     int b = 0;
-    bool any = false;  // an item with work came before (its O must be released first)
-    for (int r = 0; r * static_cast<int>(gridDim.x) < n_items; ++r) {
-      const int w = wave_item(r);
-      if (w >= n_items) continue;
-      const int n_tiles = item_at(w, p).n_tiles;
+    bool any = false;  // a unit with work came before (its O must be released first)
+    sched::Walker walk(p.plan, static_cast<int>(blockIdx.x));
+    sched::Unit u;
+    while (walk.next(u)) {
+      const int n_tiles = u.t1 - u.t0;
       if (n_tiles == 0) continue;
       released();  // Q and K_0 of this item resident
       if (leader) {
@@ -767,10 +849,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     int tt = 0;
     int nq = 0;
-    for (int r = 0; r * static_cast<int>(gridDim.x) < n_items; ++r) {
-      const int w = wave_item(r);
-      if (w >= n_items) continue;
-      const int n_tiles = item_at(w, p).n_tiles;
+    sched::Walker walk(p.plan, static_cast<int>(blockIdx.x));
+    sched::Unit u;
+    while (walk.next(u)) {
+      const int n_tiles = u.t1 - u.t0;
       if (n_tiles == 0) continue;
       if (lane == 0) {
         wait_phase(bar(BAR_Q), nq & 1, watch);

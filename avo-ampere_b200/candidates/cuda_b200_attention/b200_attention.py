@@ -45,6 +45,16 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "avo_b200_acc_to_bf16": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_ll, _c_ll, _vp]),
     "avo_b200_watchdog_selftest": (_c_int, [_c_int, _vp, _vp]),
     "avo_b200_exp2_poly_eval": (_c_int, [_vp, _vp, _c_ll, _vp]),
+    "avo_b200_attn_workspace_size": (_c_int, [ctypes.POINTER(ctypes.c_size_t)]),
+    "avo_b200_attn_fwd_ws": (
+        _c_int,
+        [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _vp, ctypes.c_size_t,
+         _vp, _vp],
+    ),
+    "avo_b200_schedule_units": (
+        _c_int,
+        [_c_int, _c_int, _c_int, _c_int, _c_ll, _c_ll, _c_int, _c_int, _vp, _vp, _c_int, _vp],
+    ),
     "avo_b200_attn_fwd_split_noalloc": (
         _c_int,
         [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp, _vp],
@@ -65,6 +75,7 @@ class B200AttentionError(RuntimeError):
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
 _status_words: dict[int, Any] = {}
+_workspaces: dict[int, Any] = {}
 
 
 def _build_module():
@@ -138,12 +149,35 @@ def status_word(device) -> Any:
     return word
 
 
+def workspace(device) -> Any:
+    """Per-device scratch for split work items (uint8, zero-filled once at allocation; the
+    kernel leaves it zeroed after every launch that completes).  Allocated by torch's
+    caching allocator on first use and kept for the life of the process."""
+    torch = _torch()
+    index = torch.device(device).index
+    if index is None:
+        index = torch.cuda.current_device()
+    ws = _workspaces.get(index)
+    if ws is None:
+        size = ctypes.c_size_t(0)
+        with torch.cuda.device(index):
+            _check(load_library().avo_b200_attn_workspace_size(ctypes.byref(size)),
+                   "avo_b200_attn_workspace_size")
+        ws = torch.zeros(int(size.value), dtype=torch.uint8, device=f"cuda:{index}")
+        _workspaces[index] = ws
+    return ws
+
+
 def check_status(device, *, reset: bool = True) -> int:
-    """Synchronize ``device``'s status word; raise if a kernel reported an abort."""
+    """Synchronize ``device``'s status word; raise if a kernel reported an abort.  After an
+    abort the device's split-piece workspace is zeroed again (its flags may be stale)."""
     word = status_word(device)
     value = int(word.item())
     if reset and value:
         word.zero_()
+        index = word.device.index
+        if index in _workspaces:
+            _workspaces[index].zero_()
     if value & (STATUS_WATCHDOG | STATUS_DRAIN):
         raise B200AttentionError(
             f"device watchdog fired (status {value}): a kernel pipeline wait timed out; "
@@ -181,8 +215,13 @@ def default_scale(head_dim: int = HEAD_DIM) -> float:
 
 
 def attention_forward(q, k, v, causal: bool, *, softmax_scale: float | None = None,
-                      need_lse: bool = True, out=None, lse=None):
-    """O (bf16, like q) and LSE (fp32 [B, H, S], natural log, or None) of SDPA."""
+                      need_lse: bool = True, out=None, lse=None, split: bool = True):
+    """O (bf16, like q) and LSE (fp32 [B, H, S], natural log, or None) of SDPA.
+
+    With ``split`` (the default) the call goes through ``avo_b200_attn_fwd_ws`` with the
+    device's workspace, which lets the kernel cut work items between CTAs where whole
+    items would leave SMs idle (and order causal work by head groups); ``split=False``
+    calls ``avo_b200_attn_fwd``, whole items only."""
     torch = _torch()
     _validate(q, k, v)
     batch, heads, seq, head_dim = (int(x) for x in q.shape)
@@ -195,13 +234,22 @@ def attention_forward(q, k, v, causal: bool, *, softmax_scale: float | None = No
     scale = default_scale(head_dim) if softmax_scale is None else float(softmax_scale)
     lib = load_library()
     with torch.cuda.device(q.device):
-        code = lib.avo_b200_attn_fwd(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
-            lse.data_ptr() if lse is not None else None,
-            batch, heads, seq, head_dim, 1 if causal else 0, scale,
-            status_word(q.device).data_ptr(), _stream_handle(q.device),
-        )
-    _check(code, "avo_b200_attn_fwd")
+        if split:
+            ws = workspace(q.device)
+            code = lib.avo_b200_attn_fwd_ws(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                lse.data_ptr() if lse is not None else None,
+                batch, heads, seq, head_dim, 1 if causal else 0, scale, ws.data_ptr(), ws.numel(),
+                status_word(q.device).data_ptr(), _stream_handle(q.device),
+            )
+        else:
+            code = lib.avo_b200_attn_fwd(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                lse.data_ptr() if lse is not None else None,
+                batch, heads, seq, head_dim, 1 if causal else 0, scale,
+                status_word(q.device).data_ptr(), _stream_handle(q.device),
+            )
+    _check(code, "avo_b200_attn_fwd_ws" if split else "avo_b200_attn_fwd")
     return out, lse
 
 
@@ -340,3 +388,26 @@ def exp2_poly_eval(x):
         code = lib.avo_b200_exp2_poly_eval(x.data_ptr(), y.data_ptr(), x.numel(), _stream_handle(x.device))
     _check(code, "avo_b200_exp2_poly_eval")
     return y
+
+
+def schedule_units(num_bh: int, seq_q: int, seq_kv: int, causal: bool, *, sm_count: int = 148,
+                   split: bool = True, q_pos0: int = 0, kv_pos0: int = 0, max_units: int = 512):
+    """The kernel's work plan, enumerated on the host (no GPU needed): returns
+    (mode, grid, group_pairs, wave_items, units) where units[c] lists CTA c's units as
+    (bh, q0, t0, t1, kind, seg, cont_lo, cont_hi) in processing order."""
+    import numpy as np
+
+    lib = load_library()
+    plan = (ctypes.c_int * 4)()
+    code = lib.avo_b200_schedule_units(num_bh, seq_q, seq_kv, 1 if causal else 0, q_pos0, kv_pos0, sm_count,
+                                       1 if split else 0, plan, None, max_units, None)
+    _check(code, "avo_b200_schedule_units")
+    grid = plan[1]
+    units = np.zeros((max(grid, 1), max_units, 8), dtype=np.int32)
+    counts = np.zeros(max(grid, 1), dtype=np.int32)
+    code = lib.avo_b200_schedule_units(num_bh, seq_q, seq_kv, 1 if causal else 0, q_pos0, kv_pos0, sm_count,
+                                       1 if split else 0, plan, units.ctypes.data, max_units, counts.ctypes.data)
+    _check(code, "avo_b200_schedule_units")
+    if (counts > max_units).any():
+        raise ValueError(f"more than {max_units} units per CTA")
+    return plan[0], grid, plan[2], plan[3], [units[c, :counts[c]].tolist() for c in range(grid)]

@@ -32,6 +32,8 @@
 #ifndef AVO_B200_ATTN_H_
 #define AVO_B200_ATTN_H_
 
+#include <stddef.h>
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -68,6 +70,43 @@ const char* avo_b200_strerror(int code);
 int avo_b200_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int batch,
                       int heads, int seq, int head_dim, int causal, float softmax_scale,
                       int* status_dev, void* stream);
+
+/*
+ * Bytes of workspace avo_b200_attn_fwd_ws wants on the current device (it grows with the
+ * multiprocessor count: about 38.5 MB on a 148-SM B200).  No reference counterpart.
+ */
+int avo_b200_attn_workspace_size(size_t* bytes);
+
+/*
+ * avo_b200_attn_fwd with caller-provided scratch (a workspace, as cuDNN and
+ * FlashAttention take one; no reference counterpart: the reference's single-GPU seeds
+ * need none).  With it the kernel may cut a work item's key/value range between CTAs
+ * (stream-K) where whole items would leave multiprocessors idle, e.g. one GPU's head
+ * shard of a problem split over 8 GPUs, and orders causal work by groups of heads
+ * whose K/V stay in L2; the pieces are merged by log-sum-exp inside the same launch
+ * (a cooperative launch: all CTAs resident).  Same arguments and results as
+ * avo_b200_attn_fwd otherwise.  workspace: device memory of at least
+ * avo_b200_attn_workspace_size() bytes, 256-byte aligned, ZERO-FILLED before its first
+ * use; every launch that completes leaves it zeroed again, so it is reused as is, but
+ * after a watchdog abort it must be zeroed again.  Launches that share one workspace
+ * must not overlap in time.  workspace == NULL behaves exactly like avo_b200_attn_fwd.
+ */
+int avo_b200_attn_fwd_ws(const void* q, const void* k, const void* v, void* o, float* lse, int batch,
+                         int heads, int seq, int head_dim, int causal, float softmax_scale, void* workspace,
+                         size_t workspace_bytes, int* status_dev, void* stream);
+
+/*
+ * Diagnostic (no reference counterpart; host only, needs no GPU): the work plan the
+ * kernel would run for these sizes on `sm_count` multiprocessors, with (split != 0) or
+ * without a workspace.  plan_out[4] = {mode (0 whole items in waves, 1 waves + split
+ * tail, 2 causal head groups), CTAs, pairs per group, items in waves}.  If units and
+ * counts are non-null, CTA c's units go to units[(c * max_units + n) * 8 ...] as
+ * {bh, q0, t0, t1, kind (0 whole, 1 first piece, 2 continuation), segment, first and
+ * last CTA holding continuation pieces} and counts[c] = its number of units (only the
+ * first max_units are stored).
+ */
+int avo_b200_schedule_units(int num_bh, int seq_q, int seq_kv, int causal, long long q_pos0, long long kv_pos0,
+                            int sm_count, int split, int* plan_out, int* units, int max_units, int* counts);
 
 /*
  * Block form used by the context-parallel ring (no reference counterpart: the
