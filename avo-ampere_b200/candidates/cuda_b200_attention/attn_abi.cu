@@ -403,7 +403,7 @@ extern "C" int avo_b200_schedule_units(int num_bh, int seq_q, int seq_kv, int ca
       sched::make_plan(num_bh, seq_q, seq_kv, causal, q_pos0, kv_pos0, sm_count, split != 0);
   plan_out[0] = plan.mode;
   plan_out[1] = plan.grid;
-  plan_out[2] = plan.group_pairs;
+  plan_out[2] = plan.run_min;
   plan_out[3] = plan.wave_items;
   if (units == nullptr || counts == nullptr) return AVO_B200_OK;
   for (int c = 0; c < plan.grid; ++c) {

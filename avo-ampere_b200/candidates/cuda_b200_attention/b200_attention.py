@@ -220,8 +220,8 @@ def attention_forward(q, k, v, causal: bool, *, softmax_scale: float | None = No
 
     With ``split`` (the default) the call goes through ``avo_b200_attn_fwd_ws`` with the
     device's workspace, which lets the kernel cut work items between CTAs where whole
-    items would leave SMs idle (and order causal work by head groups); ``split=False``
-    calls ``avo_b200_attn_fwd``, whole items only."""
+    items would leave SMs idle; ``split=False`` calls ``avo_b200_attn_fwd``, whole items
+    only."""
     torch = _torch()
     _validate(q, k, v)
     batch, heads, seq, head_dim = (int(x) for x in q.shape)
@@ -393,7 +393,7 @@ def exp2_poly_eval(x):
 def schedule_units(num_bh: int, seq_q: int, seq_kv: int, causal: bool, *, sm_count: int = 148,
                    split: bool = True, q_pos0: int = 0, kv_pos0: int = 0, max_units: int = 512):
     """The kernel's work plan, enumerated on the host (no GPU needed): returns
-    (mode, grid, group_pairs, wave_items, units) where units[c] lists CTA c's units as
+    (mode, grid, run_min, wave_items, units) where units[c] lists CTA c's units as
     (bh, q0, t0, t1, kind, seg, cont_lo, cont_hi) in processing order."""
     import numpy as np
 

@@ -5,21 +5,16 @@
 //
 // A work item is 256 query rows (two 128-row Q tiles) of one (batch, head) pair; it
 // needs n KV tiles of 128 keys.  A unit is an item restricted to KV tiles [t0, t1).
-// Three plans:
+// Two plans:
 //
 //   kWaves   every item whole, CTA c takes one item per wave of `grid` items, walking
 //            the waves in alternating directions.  Causal items are ordered longest
-//            first over all heads (balances the decreasing lengths).
+//            first over all heads (balances the decreasing lengths within ~2 %).
 //   kTail    non-causal: the first F full waves as above, then the remaining R < grid
 //            items ("the tail") as one stream-K segment: their tiles, concatenated in
-//            item order, are cut into `grid` equal runs, one per CTA.  Used when whole
-//            items would leave a large share of the SMs idle in the last wave (few items
-//            per SM, e.g. one head shard of a problem split over 8 GPUs).
-//   kGroups  causal (same query and key positions): heads are taken in groups of
-//            `group_pairs` (batch, head) pairs whose K/V fit comfortably in L2, and each
-//            group is one stream-K segment, q blocks ascending within each pair.  Every
-//            CTA gets the same number of tiles per group whatever the item lengths, and
-//            the CTAs work on one group's K/V at a time.
+//            item order, are cut into equal runs, one per CTA.  Used when whole items
+//            would leave a large share of the SMs idle in the last wave (few items per
+//            SM, e.g. one head shard of a problem split over 8 GPUs).
 //
 // In a stream-K segment an item can be cut between consecutive CTAs.  CTA c's run may
 // start inside an item (a continuation piece, written as an unnormalised partial to the
@@ -30,14 +25,12 @@
 // runs.
 #pragma once
 
-#include <cmath>
 
 namespace avo_b200 {
 namespace sched {
 
 constexpr int kWaves = 0;
 constexpr int kTail = 1;
-constexpr int kGroups = 2;
 
 constexpr int kWhole = 0;
 constexpr int kFirst = 1;  // first piece of a split item: merges the continuation pieces
@@ -57,8 +50,6 @@ struct Plan {
   long long kv_pos0;
   int seq_q;
   int wave_items;      // kTail: items [0, wave_items) go in whole-item waves
-  int group_pairs;     // kGroups: pairs per group
-  int pair_tiles;      // kGroups: KV tiles of one pair's items together
   int run_min;         // stream-K: shortest run per CTA (bounds the pieces of one item)
 };
 
@@ -98,35 +89,17 @@ __host__ __device__ inline int wave_item(int r, int cta, int grid) {
   return r * grid + ((r & 1) ? grid - 1 - cta : cta);
 }
 
-// Tiles before q block qb of a pair in the kGroups geometry (standard causal: query and
-// key positions equal, so block qb sees min(2 qb + 2, n_kv) tiles and only the last
-// block can be clipped): qb (qb + 1).
-__host__ __device__ inline long long group_prefix(int qb) { return static_cast<long long>(qb) * (qb + 1); }
-
-// q block holding tile offset `rem` of a pair (kGroups).
-__host__ __device__ inline int group_qb(const Plan& p, long long rem) {
-  // largest qb with qb (qb + 1) <= rem, at most nq - 1
-  int qb = static_cast<int>((sqrtf(4.0f * static_cast<float>(rem) + 1.0f) - 1.0f) * 0.5f);
-  while (qb > 0 && group_prefix(qb) > rem) --qb;
-  while (qb + 1 < p.nq && group_prefix(qb + 1) <= rem) ++qb;
-  return qb < p.nq - 1 ? qb : p.nq - 1;
-}
-
-// Segment geometry.  Segment s of a plan: its first item index (kTail) or pair (kGroups),
-// its total tiles, and the run length per CTA.
+// Segment geometry.  Segment s of a plan: its first item, its item count, its total tiles
+// and the run length per CTA.
 struct Segment {
   int kind;            // 0 waves, 1 stream-K
-  int first;           // kTail: first item; kGroups: first pair
-  int count;           // items (kTail) or pairs (kGroups)
+  int first;           // first item
+  int count;           // items
   long long tiles;     // stream-K: total tiles
   long long run;       // stream-K: tiles per CTA run, ceil(tiles / grid)
 };
 
-__host__ __device__ inline int num_segments(const Plan& p) {
-  if (p.mode == kWaves) return 1;
-  if (p.mode == kTail) return 2;
-  return (p.num_bh + p.group_pairs - 1) / p.group_pairs;
-}
+__host__ __device__ inline int num_segments(const Plan& p) { return p.mode == kWaves ? 1 : 2; }
 
 __host__ __device__ inline Segment segment(const Plan& p, int s) {
   Segment g{0, 0, 0, 0, 0};
@@ -135,22 +108,15 @@ __host__ __device__ inline Segment segment(const Plan& p, int s) {
     g.count = p.num_bh * p.nq;
     return g;
   }
-  if (p.mode == kTail) {
-    if (s == 0) {
-      g.kind = 0;
-      g.count = p.wave_items;
-      return g;
-    }
-    g.kind = 1;
-    g.first = p.wave_items;
-    g.count = p.num_bh * p.nq - p.wave_items;
-    g.tiles = static_cast<long long>(g.count) * p.n_kv;
-  } else {
-    g.kind = 1;
-    g.first = s * p.group_pairs;
-    g.count = p.num_bh - g.first < p.group_pairs ? p.num_bh - g.first : p.group_pairs;
-    g.tiles = static_cast<long long>(g.count) * p.pair_tiles;
+  if (s == 0) {
+    g.kind = 0;
+    g.count = p.wave_items;
+    return g;
   }
+  g.kind = 1;
+  g.first = p.wave_items;
+  g.count = p.num_bh * p.nq - p.wave_items;
+  g.tiles = static_cast<long long>(g.count) * p.n_kv;
   g.run = (g.tiles + p.grid - 1) / p.grid;
   if (g.run < p.run_min) g.run = p.run_min;
   return g;
@@ -158,29 +124,20 @@ __host__ __device__ inline Segment segment(const Plan& p, int s) {
 
 // Locates global tile `pos` of stream-K segment g: the item (bh, q0), the item's tile
 // count n, and the tile index t within the item.
-__host__ __device__ inline void locate(const Plan& p, const Segment& g, long long pos, int& bh, int& q0,
-                                       int& n, int& t) {
-  if (p.mode == kTail) {
-    const int w = g.first + static_cast<int>(pos / p.n_kv);
-    t = static_cast<int>(pos % p.n_kv);
-    bh = w / p.nq;
-    q0 = (w % p.nq) * kRowsPerItem;
-    n = p.n_kv;
-  } else {
-    bh = g.first + static_cast<int>(pos / p.pair_tiles);
-    const long long rem = pos % p.pair_tiles;
-    const int qb = group_qb(p, rem);
-    q0 = qb * kRowsPerItem;
-    t = static_cast<int>(rem - group_prefix(qb));
-    n = item_tiles(p, q0);
-  }
+__host__ __device__ inline void locate(const Plan& p, const Segment& g, int pos, int& bh, int& q0, int& n,
+                                       int& t) {
+  const int w = g.first + pos / p.n_kv;
+  t = pos % p.n_kv;
+  bh = w / p.nq;
+  q0 = (w % p.nq) * kRowsPerItem;
+  n = p.n_kv;
 }
 
 // Chooses the plan of a launch.  `split_ok`: the caller provided scratch for split pieces
 // and the launch can hold all CTAs resident at once (a cooperative launch); without it
 // every item stays whole (kWaves).  `sms`: multiprocessors, one CTA each.
 inline Plan make_plan(int num_bh, int seq_q, int seq_kv, int causal, long long q_pos0, long long kv_pos0, int sms,
-                      bool split_ok, long long kv_group_budget_bytes = 48ll << 20) {
+                      bool split_ok) {
   Plan p{};
   p.mode = kWaves;
   p.num_bh = num_bh;
@@ -195,7 +152,7 @@ inline Plan make_plan(int num_bh, int seq_q, int seq_kv, int causal, long long q
   p.run_min = 1;
   if (!split_ok || items == 0 || p.n_kv == 0 || sms <= 1) return p;
   const int run_min = (p.n_kv + 3) / 4 > 4 ? (p.n_kv + 3) / 4 : 4;
-  if (!p.causal) {
+  if (!p.causal && static_cast<long long>(items) * p.n_kv <= 0x7fffffffll) {
     // Whole items: F full waves and a last wave of R items, (F + 1) * T tiles per CTA at
     // most.  Split: the R tail items' tiles spread evenly.  Take the split when it saves
     // at least 3 % (a split piece costs about two tiles of extra epilogue work).
@@ -212,16 +169,10 @@ inline Plan make_plan(int num_bh, int seq_q, int seq_kv, int causal, long long q
     p.grid = F > 0 ? sms : static_cast<int>((R * T + run - 1) / run);
     return p;
   }
-  if (q_pos0 != kv_pos0 || seq_q != seq_kv || items < 2ll * sms) return p;
-  const long long pair_kv = static_cast<long long>(seq_kv) * 128 * 2 * 2;
-  long long g = kv_group_budget_bytes / pair_kv;
-  if (g < 1) g = 1;
-  if (g > num_bh) g = num_bh;
-  p.mode = kGroups;
-  p.group_pairs = static_cast<int>(g);
-  p.pair_tiles = (p.nq - 1) * p.nq + (2 * p.nq < p.n_kv ? 2 * p.nq : p.n_kv);
-  p.run_min = run_min;
-  p.grid = sms;
+  // Causal: whole items, longest first over all heads (balanced within ~2 % on the causal
+  // workloads).  Head-grouped stream-K plans for causal work were measured on B200 and ran
+  // 20-27 % slower: runs over a pair's first q blocks hold many 2-6 tile units, whose fixed
+  // per-unit costs the tile balance does not see.
   return p;
 }
 
@@ -232,6 +183,16 @@ class Walker {
  public:
   // `p` must outlive the walker (the kernel's parameter block).
   __host__ __device__ Walker(const Plan& p, int cta) : p_(p), cta_(cta), s_(0), r_(0), pos_(-1), end_(0) {}
+  // Resumes from a state saved with save() (the softmax warps keep it in shared memory
+  // across a unit's tile loop rather than in registers).
+  __host__ __device__ Walker(const Plan& p, int cta, int s, int r, int pos, int end)
+      : p_(p), cta_(cta), s_(s), r_(r), pos_(pos), end_(end) {}
+  __host__ __device__ void save(int* out) const {
+    out[0] = s_;
+    out[1] = r_;
+    out[2] = pos_;
+    out[3] = end_;
+  }
 
   __host__ __device__ bool next(Unit& u) {
     const int nseg = num_segments(p_);
@@ -252,25 +213,27 @@ class Walker {
         }
       } else {
         if (pos_ < 0) {
-          pos_ = static_cast<long long>(cta_) * g.run;
-          end_ = pos_ + g.run < g.tiles ? pos_ + g.run : g.tiles;
+          const long long start = static_cast<long long>(cta_) * g.run;
+          const long long stop = start + g.run < g.tiles ? start + g.run : g.tiles;
+          pos_ = static_cast<int>(start < g.tiles ? start : g.tiles);
+          end_ = static_cast<int>(stop);
         }
         if (pos_ < end_) {
           int n, t;
           locate(p_, g, pos_, u.bh, u.q0, n, t);
-          const long long item_start = pos_ - t;
-          const long long item_end = item_start + n;
-          const long long stop = end_ < item_end ? end_ : item_end;
+          const int item_start = pos_ - t;
+          const int item_end = item_start + n;
+          const int stop = end_ < item_end ? end_ : item_end;
           u.t0 = t;
-          u.t1 = t + static_cast<int>(stop - pos_);
-          u.seg = s_ - (p_.mode == kTail ? 1 : 0);
+          u.t1 = t + (stop - pos_);
+          u.seg = s_ - 1;
           u.cont_lo = u.cont_hi = -1;
           if (u.t0 > 0) {
             u.kind = kCont;
           } else if (u.t1 < n) {
             u.kind = kFirst;
             u.cont_lo = cta_ + 1;
-            u.cont_hi = static_cast<int>((item_end - 1) / g.run);
+            u.cont_hi = static_cast<int>((item_end - 1) / g.run);  // run > 0 in a stream-K segment
           } else {
             u.kind = kWhole;
           }
@@ -290,8 +253,8 @@ class Walker {
   int cta_;
   int s_;
   int r_;
-  long long pos_;
-  long long end_;
+  int pos_;   // tiles of a segment fit in int: the host refuses larger launches
+  int end_;
 };
 
 }  // namespace sched

@@ -82,8 +82,8 @@ int avo_b200_attn_workspace_size(size_t* bytes);
  * FlashAttention take one; no reference counterpart: the reference's single-GPU seeds
  * need none).  With it the kernel may cut a work item's key/value range between CTAs
  * (stream-K) where whole items would leave multiprocessors idle, e.g. one GPU's head
- * shard of a problem split over 8 GPUs, and orders causal work by groups of heads
- * whose K/V stay in L2; the pieces are merged by log-sum-exp inside the same launch
+ * shard of a problem split over 8 GPUs; the pieces are merged by log-sum-exp inside the
+ * same launch
  * (a cooperative launch: all CTAs resident).  Same arguments and results as
  * avo_b200_attn_fwd otherwise.  workspace: device memory of at least
  * avo_b200_attn_workspace_size() bytes, 256-byte aligned, ZERO-FILLED before its first
@@ -99,8 +99,8 @@ int avo_b200_attn_fwd_ws(const void* q, const void* k, const void* v, void* o, f
  * Diagnostic (no reference counterpart; host only, needs no GPU): the work plan the
  * kernel would run for these sizes on `sm_count` multiprocessors, with (split != 0) or
  * without a workspace.  plan_out[4] = {mode (0 whole items in waves, 1 waves + split
- * tail, 2 causal head groups), CTAs, pairs per group, items in waves}.  If units and
- * counts are non-null, CTA c's units go to units[(c * max_units + n) * 8 ...] as
+ * tail), CTAs, shortest split run in tiles, items in waves}.  If units and counts are
+ * non-null, CTA c's units go to units[(c * max_units + n) * 8 ...] as
  * {bh, q0, t0, t1, kind (0 whole, 1 first piece, 2 continuation), segment, first and
  * last CTA holding continuation pieces} and counts[c] = its number of units (only the
  * first max_units are stored).
