@@ -23,7 +23,7 @@ HERE = Path(__file__).resolve().parent
 LIB_NAME = "libavo_b200_attn.so"
 LIB_PATH = HERE / LIB_NAME
 SOURCES = ("attn_abi.cu",)
-HEADERS = ("attn_fwd.cuh", "sm100_ptx.cuh")
+HEADERS = ("attn_fwd.cuh", "sm100_ptx.cuh", "schedule.cuh")
 GENCODE = ("-gencode", "arch=compute_100a,code=sm_100a")
 NVCC_FLAGS = (
     *GENCODE,

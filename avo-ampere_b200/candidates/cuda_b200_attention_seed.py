@@ -26,6 +26,7 @@ _BINDING = "avo_b200_attention_binding"
 
 AVO_SOURCE_FILES = (
     "cuda_b200_attention/sm100_ptx.cuh",
+    "cuda_b200_attention/schedule.cuh",
     "cuda_b200_attention/attn_fwd.cuh",
     "cuda_b200_attention/attn_abi.cu",
     "cuda_b200_attention/b200_attention.py",
