@@ -119,6 +119,8 @@ NAMED_CASES: dict[str, AttentionCase] = {
     "b1_h16_s32768_causal": AttentionCase(seq_len=32768, causal=True, total_tokens=32768),
     # Throughput target point: B4 H16 S8192 non-causal.
     "b4_h16_s8192_noncausal": AttentionCase(seq_len=8192, causal=False, total_tokens=32768),
+    # One GPU's head shard of the target point at 8 GPUs (8 of its 64 pairs).
+    "b1_h8_s8192_noncausal": AttentionCase(seq_len=8192, causal=False, num_heads=8, total_tokens=8192),
 }
 
 
