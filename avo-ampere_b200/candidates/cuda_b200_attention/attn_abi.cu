@@ -118,6 +118,11 @@ EncodeTiledFn g_encode = nullptr;
 int g_device_state[kMaxDevices] = {};  // 0 unchecked, 1 ready, -1 not a B200
 int g_sm_count[kMaxDevices] = {};      // multiprocessors, read once per device
 
+// Pipeline-wait limit (AVO_B200_WATCHDOG_MS, default 2 s).  It is wall-clock time
+// (%globaltimer): on a GPU time-sliced between contexts (another process's work scheduled
+// in between), a wait can also run out because this context was switched out that long;
+// the launch then reports the watchdog bit although nothing was wrong.  Raise the limit on
+// such shared GPUs.
 unsigned long long watchdog_limit_ns() {
   static const unsigned long long limit = [] {
     const char* env = std::getenv("AVO_B200_WATCHDOG_MS");
@@ -188,11 +193,11 @@ int prepare_device(int* sm_count = nullptr) {
   // works out if the launch allocation is exactly the one the split was computed for;
   // otherwise an increase could wait forever.  Refuse to launch in that case.
   cudaFuncAttributes attr{};
-  if (cudaFuncGetAttributes(&attr, attn_fwd_kernel) != cudaSuccess ||
-      attr.numRegs != static_cast<int>(kRegsLaunch)) {
+  if (cudaFuncGetAttributes(&attr, attn_fwd_kernel) != cudaSuccess) {
     (void)cudaGetLastError();
     return AVO_B200_ELAUNCH;
   }
+  if (attr.numRegs != static_cast<int>(kRegsLaunch)) return AVO_B200_EREGS;
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
     (void)cudaGetLastError();
@@ -357,6 +362,9 @@ extern "C" const char* avo_b200_strerror(int code) {
     case AVO_B200_ELAUNCH: return "CUDA launch error";
     case AVO_B200_ETENSORMAP: return "tensor map encoding failed";
     case AVO_B200_EDRIVER: return "driver entry point cuTensorMapEncodeTiled unavailable";
+    case AVO_B200_EREGS:
+      return "attention kernel built with an unexpected register count (the setmaxnreg split needs 168 per "
+             "thread at launch); rebuild the library";
     case AVO_B200_ETOOBIG:
       return "problem too large for the no-allocation entry point (batch*heads*seq > 16384 rows)";
     default: return "unknown error";

@@ -66,6 +66,7 @@ STATUS_WATCHDOG = 1
 STATUS_DRAIN = 2
 NOALLOC_MAX_ROWS = 16384  # AVO_B200_NOALLOC_MAX_ROWS
 ETOOBIG = 6
+EREGS = 7
 
 
 class B200AttentionError(RuntimeError):

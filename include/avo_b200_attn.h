@@ -23,6 +23,10 @@
  *   AVO_B200_ETENSORMAP        4  cuTensorMapEncodeTiled rejected a descriptor
  *   AVO_B200_EDRIVER           5  driver entry point for tensor maps unavailable
  *   AVO_B200_ETOOBIG           6  problem exceeds the static scratch of the no-allocation entry
+ *   AVO_B200_EREGS             7  the built kernel's register allocation is not the one its
+ *                                 per-warpgroup register split (setmaxnreg) was computed for; the
+ *                                 library was built by a compiler that allocated differently and
+ *                                 refuses to launch (rebuild with the nvcc this file was tuned on)
  *
  * Device status bits (written asynchronously into *status_dev when non-null; the
  * caller zeroes the word and reads it after synchronizing):
@@ -45,6 +49,7 @@ extern "C" {
 #define AVO_B200_ETENSORMAP 4
 #define AVO_B200_EDRIVER 5
 #define AVO_B200_ETOOBIG 6
+#define AVO_B200_EREGS 7
 
 /* Row capacity (batch * heads * seq) of avo_b200_attn_fwd_split_noalloc's scratch. */
 #define AVO_B200_NOALLOC_MAX_ROWS 16384

@@ -44,6 +44,7 @@ def test_abi_version_and_strerror(b200):
     assert "invalid" in b200.strerror(1)
     assert "B200" in b200.strerror(2)
     assert b200.strerror(99) == "unknown error"
+    assert "register count" in b200.strerror(7) and "168" in b200.strerror(7)
 
 
 def test_library_links_no_driver_library(b200):
