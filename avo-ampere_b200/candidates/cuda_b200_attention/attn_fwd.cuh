@@ -258,16 +258,16 @@ __device__ __forceinline__ void exp_half(const uint32_t (&sa)[32], const uint32_
 
 // exp_half over keys 0-63 with the row max over all 128 scores (raw, unscaled) folded
 // into the same straight-line block: every pair step also folds two score pairs into
-// eight running maxima, so the independent max3 work fills the gaps between dependent
+// four running maxima, so the independent max3 work fills the gaps between dependent
 // MUFU operations.  Measured on B200 with one warp per SM sub-partition: 565 cycles
 // for this half in one block, about 840 when a branch split the exps from a separate
 // max loop (the scheduler cannot interleave across basic blocks).
 __device__ __forceinline__ float exp_half_max(const uint32_t (&s)[4][32], uint64_t scale2, uint64_t neg_m2,
                                               uint64_t (&sum2)[kSumAcc], uint32_t tP) {
   uint32_t pk[8];
-  float mx[8];
+  float mx[4];  // four running maxima (eight measured 0.5 % slower: more live registers)
 #pragma unroll
-  for (int e = 0; e < 8; ++e) mx[e] = -CUDART_INF_F;
+  for (int e = 0; e < 4; ++e) mx[e] = -CUDART_INF_F;
 #pragma unroll
   for (int q = 0; q < 32; ++q) {
     const int cc = q >> 4, e = (q & 15) * 2;
@@ -286,10 +286,10 @@ __device__ __forceinline__ float exp_half_max(const uint32_t (&s)[4][32], uint64
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const int pr = 2 * q + r, c = pr >> 4, ee = (pr & 15) * 2;
-      mx[pr & 7] = fmax3(mx[pr & 7], u2f(s[c][ee]), u2f(s[c][ee + 1]));
+      mx[pr & 3] = fmax3(mx[pr & 3], u2f(s[c][ee]), u2f(s[c][ee + 1]));
     }
   }
-  return fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+  return fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
 }
 
 // Flag of a split-piece slot: poll with acquire semantics until it holds `want`, bounded
