@@ -184,20 +184,24 @@ int prepare_device(int* sm_count = nullptr) {
     if (dev < kMaxDevices) g_device_state[dev] = -1;
     return AVO_B200_ENODEV;
   }
-  if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-      cudaSuccess) {
+  if (cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+          cudaSuccess) {
     (void)cudaGetLastError();
     return AVO_B200_ELAUNCH;
   }
   // The kernel rebalances registers between warpgroups with setmaxnreg, which only
   // works out if the launch allocation is exactly the one the split was computed for;
   // otherwise an increase could wait forever.  Refuse to launch in that case.
-  cudaFuncAttributes attr{};
-  if (cudaFuncGetAttributes(&attr, attn_fwd_kernel) != cudaSuccess) {
+  cudaFuncAttributes attr{}, attr_t{};
+  if (cudaFuncGetAttributes(&attr, attn_fwd_kernel<false>) != cudaSuccess ||
+      cudaFuncGetAttributes(&attr_t, attn_fwd_kernel<true>) != cudaSuccess) {
     (void)cudaGetLastError();
     return AVO_B200_ELAUNCH;
   }
-  if (attr.numRegs != static_cast<int>(kRegsLaunch)) return AVO_B200_EREGS;
+  if (attr.numRegs != static_cast<int>(kRegsLaunch) || attr_t.numRegs != static_cast<int>(kRegsLaunch))
+    return AVO_B200_EREGS;
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
     (void)cudaGetLastError();
@@ -265,6 +269,42 @@ SplitScratch carve_workspace(void* ws, int sms) {
   return s;
 }
 
+// Plans, with kTable's item lists, for the last few launch shapes (building the lists is
+// a greedy pass per candidate group size: worth doing once per shape, not per launch).
+struct PlanEntry {
+  long long key[8];
+  sched::Plan plan;
+  TableParam<true> table;
+};
+constexpr int kPlanCache = 8;
+PlanEntry g_plans[kPlanCache];
+int g_plans_used = 0;
+int g_plans_next = 0;
+
+// Returns a copy (this thread's own) of the cached entry: another thread may replace the
+// cache slot as soon as the lock is released.
+const PlanEntry& cached_plan(int num_bh, int seq_q, int seq_kv, int causal, long long q_pos0, long long kv_pos0,
+                             int sms, bool split_ok) {
+  static thread_local PlanEntry mine;
+  const long long key[8] = {num_bh, seq_q, seq_kv, causal ? 1 : 0, q_pos0, kv_pos0, sms, split_ok ? 1 : 0};
+  std::lock_guard<std::mutex> lock(g_mu);
+  for (int e = 0; e < g_plans_used; ++e) {
+    bool same = true;
+    for (int i = 0; i < 8; ++i) same = same && g_plans[e].key[i] == key[i];
+    if (same) {
+      mine = g_plans[e];
+      return mine;
+    }
+  }
+  PlanEntry& entry = g_plans[g_plans_next];
+  g_plans_next = (g_plans_next + 1) % kPlanCache;
+  if (g_plans_used < kPlanCache) ++g_plans_used;
+  for (int i = 0; i < 8; ++i) entry.key[i] = key[i];
+  entry.plan = sched::make_plan(num_bh, seq_q, seq_kv, causal, q_pos0, kv_pos0, sms, split_ok, &entry.table.t);
+  mine = entry;
+  return mine;
+}
+
 int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int num_bh,
                int seq_q, int seq_kv, int head_dim, long long q_hs, long long kv_hs, long long o_hs,
                long long lse_hs, int causal, float scale, long long q_pos0, long long kv_pos0,
@@ -295,8 +335,8 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   const bool split_ok = workspace != nullptr && cooperative_ok();
   if (workspace != nullptr && workspace_bytes < workspace_bytes_for(sm_count)) return AVO_B200_EINVAL;
   if (workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return AVO_B200_EINVAL;
-  const sched::Plan plan =
-      sched::make_plan(num_bh, seq_q, seq_kv, causal, q_pos0, kv_pos0, sm_count, split_ok);
+  const PlanEntry& entry = cached_plan(num_bh, seq_q, seq_kv, causal, q_pos0, kv_pos0, sm_count, split_ok);
+  const sched::Plan plan = entry.plan;
   const int grid = plan.grid;
 
   alignas(64) CUtensorMap tm_q, tm_k, tm_v;
@@ -329,16 +369,21 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale * 1.4426950408889634f;
 
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (plan.mode == sched::kWaves) {
-    attn_fwd_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
-        tm_q, tm_k, tm_v, p);
+    attn_fwd_kernel<false><<<static_cast<unsigned>(grid), kThreads, kSmemBytes, st>>>(tm_q, tm_k, tm_v, p,
+                                                                                       TableParam<false>{0});
+  } else if (plan.mode == sched::kTable) {
+    attn_fwd_kernel<true><<<static_cast<unsigned>(grid), kThreads, kSmemBytes, st>>>(tm_q, tm_k, tm_v, p,
+                                                                                      entry.table);
   } else {
     // Split pieces: a CTA that merges an item waits for its neighbours' continuation
     // pieces, so every CTA must be resident at once; a cooperative launch guarantees it
     // (or fails to launch).
-    void* args[] = {&tm_q, &tm_k, &tm_v, &p};
-    if (cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(attn_fwd_kernel), dim3(grid), dim3(kThreads),
-                                    args, kSmemBytes, static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+    TableParam<false> none{0};
+    void* args[] = {&tm_q, &tm_k, &tm_v, &p, &none};
+    if (cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(attn_fwd_kernel<false>), dim3(grid),
+                                    dim3(kThreads), args, kSmemBytes, st) != cudaSuccess) {
       (void)cudaGetLastError();
       return AVO_B200_ELAUNCH;
     }
@@ -407,15 +452,16 @@ extern "C" int avo_b200_schedule_units(int num_bh, int seq_q, int seq_kv, int ca
                                        int* units, int max_units, int* counts) {
   if (num_bh < 0 || seq_q < 0 || seq_kv < 0 || sm_count <= 0 || plan_out == nullptr || max_units < 0)
     return AVO_B200_EINVAL;
+  static thread_local sched::Table table;
   const sched::Plan plan =
-      sched::make_plan(num_bh, seq_q, seq_kv, causal, q_pos0, kv_pos0, sm_count, split != 0);
+      sched::make_plan(num_bh, seq_q, seq_kv, causal, q_pos0, kv_pos0, sm_count, split != 0, &table);
   plan_out[0] = plan.mode;
   plan_out[1] = plan.grid;
-  plan_out[2] = plan.run_min;
+  plan_out[2] = plan.mode == sched::kTable ? plan.group_pairs : plan.run_min;
   plan_out[3] = plan.wave_items;
   if (units == nullptr || counts == nullptr) return AVO_B200_OK;
   for (int c = 0; c < plan.grid; ++c) {
-    sched::Walker walk(plan, c);
+    sched::Walker walk(plan, c, &table);
     sched::Unit u;
     int n = 0;
     while (walk.next(u)) {

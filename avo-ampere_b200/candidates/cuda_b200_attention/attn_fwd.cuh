@@ -323,9 +323,24 @@ __device__ __forceinline__ bool wait_flag(const int* flag, int want, const Watch
 // next unit's Q as soon as the current unit's last S MMAs have read Q, and the MMA warp
 // computes the next unit's first S tiles while the softmax warpgroups finish the current
 // unit's epilogue.
+// The kTable plan's item lists ride in the parameter block of their own instantiation, so
+// launches of the other plans carry no 25 KB table.
+template <bool kWithTable>
+struct TableParam {
+  int unused;
+};
+template <>
+struct TableParam<true> {
+  sched::Table t;
+};
+
+template <bool kWithTable>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ AttnParams p) {
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ AttnParams p,
+                    const __grid_constant__ TableParam<kWithTable> tab) {
+  const sched::Table* table = nullptr;
+  if constexpr (kWithTable) table = &tab.t;
   extern __shared__ uint8_t smem_dyn[];
   const uint32_t raw = smem_addr(smem_dyn);
   uint8_t* smem = smem_dyn + ((1024u - (raw & 1023u)) & 1023u);
@@ -397,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     while (true) {
       int n_tiles, row_keys, warp_keys;
       {
-        sched::Walker walk(p.plan, static_cast<int>(blockIdx.x), wst[0], wst[1], wst[2], wst[3]);
+        sched::Walker walk(p.plan, static_cast<int>(blockIdx.x), wst[0], wst[1], wst[2], wst[3], table);
         sched::Unit u;
         const bool more = walk.next(u);
         __syncwarp();
@@ -735,7 +750,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // No separate L2 prefetch of K/V: measured on B200 it cost 1-2 % here (the prefetch
       // operations share the TMA unit with the loads), the CTAs of a head reading the same
       // tiles close together in time already hit L2.
-      sched::Walker walk(p.plan, static_cast<int>(blockIdx.x));
+      sched::Walker walk(p.plan, static_cast<int>(blockIdx.x), table);
       sched::Unit u;
       while (!stop && walk.next(u)) {
         const int n_tiles = u.t1 - u.t0;
@@ -832,7 +847,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // keeps the issue code between barrier and MMA minimal.
     int b = 0;
     bool any = false;  // a unit with work came before (its O must be released first)
-    sched::Walker walk(p.plan, static_cast<int>(blockIdx.x));
+    sched::Walker walk(p.plan, static_cast<int>(blockIdx.x), table);
     sched::Unit u;
     while (walk.next(u)) {
       const int n_tiles = u.t1 - u.t0;
@@ -924,7 +939,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     int tt = 0;
     int nq = 0;
-    sched::Walker walk(p.plan, static_cast<int>(blockIdx.x));
+    sched::Walker walk(p.plan, static_cast<int>(blockIdx.x), table);
     sched::Unit u;
     while (walk.next(u)) {
       const int n_tiles = u.t1 - u.t0;

@@ -5,7 +5,7 @@
 //
 // A work item is 256 query rows (two 128-row Q tiles) of one (batch, head) pair; it
 // needs n KV tiles of 128 keys.  A unit is an item restricted to KV tiles [t0, t1).
-// Two plans:
+// Three plans:
 //
 //   kWaves   every item whole, CTA c takes one item per wave of `grid` items, walking
 //            the waves in alternating directions.  Causal items are ordered longest
@@ -15,6 +15,12 @@
 //            item order, are cut into equal runs, one per CTA.  Used when whole items
 //            would leave a large share of the SMs idle in the last wave (few items per
 //            SM, e.g. one head shard of a problem split over 8 GPUs).
+//   kTable   causal, many items: whole items, greedy list scheduling (each item to the
+//            CTA with the least work so far) over an order that takes the (batch, head)
+//            pairs in groups whose K/V fit in L2 and, within a group, the longest query
+//            blocks first.  The CTAs stay as balanced as with kWaves while the K/V read at
+//            any moment belong to one or two groups instead of every pair.  The host
+//            computes each CTA's item list; it travels in the kernel's parameter block.
 //
 // In a stream-K segment an item can be cut between consecutive CTAs.  CTA c's run may
 // start inside an item (a continuation piece, written as an unnormalised partial to the
@@ -31,6 +37,17 @@ namespace sched {
 
 constexpr int kWaves = 0;
 constexpr int kTail = 1;
+constexpr int kTable = 2;
+
+// kTable's item lists: CTA c takes items item[start[c] .. start[c + 1]) in order, each an
+// index into the grouped order (decode_grouped).  25 KB, within the 32 KB a kernel
+// parameter block may hold.
+constexpr int kTableCtas = 160;
+constexpr int kTableItems = 12288;
+struct Table {
+  unsigned short start[kTableCtas + 1];
+  unsigned short item[kTableItems];
+};
 
 constexpr int kWhole = 0;
 constexpr int kFirst = 1;  // first piece of a split item: merges the continuation pieces
@@ -51,6 +68,7 @@ struct Plan {
   int seq_q;
   int wave_items;      // kTail: items [0, wave_items) go in whole-item waves
   int run_min;         // stream-K: shortest run per CTA (bounds the pieces of one item)
+  int group_pairs;     // kTable: pairs per group of the grouped order
 };
 
 struct Unit {
@@ -84,6 +102,26 @@ __host__ __device__ inline void wave_order_item(const Plan& p, int w, int& bh, i
   q0 = qb * kRowsPerItem;
 }
 
+// Item k of kTable's grouped order: groups of group_pairs pairs (the last one may be
+// smaller), within a group query blocks from the last down, pairs within a block.
+__host__ __device__ inline void decode_grouped(const Plan& p, int k, int& bh, int& q0) {
+  const int g = p.group_pairs;
+  const int full = p.num_bh / g;
+  const int per_group = g * p.nq;
+  int first_pair, size, r;
+  if (k < full * per_group) {
+    first_pair = (k / per_group) * g;
+    size = g;
+    r = k % per_group;
+  } else {
+    first_pair = full * g;
+    size = p.num_bh - first_pair;
+    r = k - full * per_group;
+  }
+  bh = first_pair + r % size;
+  q0 = (p.nq - 1 - r / size) * kRowsPerItem;
+}
+
 // Item of CTA `cta` in wave r: alternating directions.
 __host__ __device__ inline int wave_item(int r, int cta, int grid) {
   return r * grid + ((r & 1) ? grid - 1 - cta : cta);
@@ -99,7 +137,7 @@ struct Segment {
   long long run;       // stream-K: tiles per CTA run, ceil(tiles / grid)
 };
 
-__host__ __device__ inline int num_segments(const Plan& p) { return p.mode == kWaves ? 1 : 2; }
+__host__ __device__ inline int num_segments(const Plan& p) { return p.mode == kTail ? 2 : 1; }
 
 __host__ __device__ inline Segment segment(const Plan& p, int s) {
   Segment g{0, 0, 0, 0, 0};
@@ -136,8 +174,64 @@ __host__ __device__ inline void locate(const Plan& p, const Segment& g, int pos,
 // Chooses the plan of a launch.  `split_ok`: the caller provided scratch for split pieces
 // and the launch can hold all CTAs resident at once (a cooperative launch); without it
 // every item stays whole (kWaves).  `sms`: multiprocessors, one CTA each.
+// kTable's lists for group size g: greedy list scheduling of the grouped order, each
+// item's cost its tile count plus one tile of fixed per-item work.  Returns the largest
+// CTA load; fills `t` if non-null.
+inline long long build_table(const Plan& p, int g, Table* t) {
+  Plan q = p;
+  q.group_pairs = g;
+  const int items = p.num_bh * p.nq;
+  // Binary min-heap of (load, CTA), ties to the lower CTA index.
+  long long hl[kTableCtas];
+  int hc[kTableCtas];
+  int count[kTableCtas];
+  int n = p.grid;
+  for (int c = 0; c < n; ++c) {
+    hl[c] = 0;
+    hc[c] = c;
+    count[c] = 0;
+  }
+  auto less = [&](int a, int b) { return hl[a] < hl[b] || (hl[a] == hl[b] && hc[a] < hc[b]); };
+  auto swap_at = [&](int a, int b) {
+    const long long l = hl[a];
+    hl[a] = hl[b];
+    hl[b] = l;
+    const int c = hc[a];
+    hc[a] = hc[b];
+    hc[b] = c;
+  };
+  static thread_local unsigned short owner[kTableItems];
+  for (int k = 0; k < items; ++k) {
+    int bh, q0;
+    decode_grouped(q, k, bh, q0);
+    const int cta = hc[0];
+    owner[k] = static_cast<unsigned short>(cta);
+    ++count[cta];
+    hl[0] += item_tiles(q, q0) + 1;
+    for (int i = 0;;) {  // sift down
+      const int a = 2 * i + 1, b = a + 1;
+      int m = i;
+      if (a < n && less(a, m)) m = a;
+      if (b < n && less(b, m)) m = b;
+      if (m == i) break;
+      swap_at(i, m);
+      i = m;
+    }
+  }
+  long long worst = 0;
+  for (int c = 0; c < n; ++c) worst = hl[c] > worst ? hl[c] : worst;
+  if (t != nullptr) {
+    t->start[0] = 0;
+    for (int c = 0; c < n; ++c) t->start[c + 1] = static_cast<unsigned short>(t->start[c] + count[c]);
+    int fill[kTableCtas];
+    for (int c = 0; c < n; ++c) fill[c] = t->start[c];
+    for (int k = 0; k < items; ++k) t->item[fill[owner[k]]++] = static_cast<unsigned short>(k);
+  }
+  return worst;
+}
+
 inline Plan make_plan(int num_bh, int seq_q, int seq_kv, int causal, long long q_pos0, long long kv_pos0, int sms,
-                      bool split_ok) {
+                      bool split_ok, Table* table = nullptr) {
   Plan p{};
   p.mode = kWaves;
   p.num_bh = num_bh;
@@ -169,10 +263,40 @@ inline Plan make_plan(int num_bh, int seq_q, int seq_kv, int causal, long long q
     p.grid = F > 0 ? sms : static_cast<int>((R * T + run - 1) / run);
     return p;
   }
-  // Causal: whole items, longest first over all heads (balanced within ~2 % on the causal
-  // workloads).  Head-grouped stream-K plans for causal work were measured on B200 and ran
-  // 20-27 % slower: runs over a pair's first q blocks hold many 2-6 tile units, whose fixed
+  // Causal: whole items.  With a workspace (split_ok, checked above: launches without one
+  // keep the longest-first waves), room for kTable's lists and at least two items per SM,
+  // the grouped greedy plan: the smallest group whose pairs' K/V fit in 48 MB among those
+  // within 2 % of the best makespan over all group sizes; otherwise longest first over all
+  // heads in waves (within ~2 % of the mean tile count per CTA on the causal workloads).
+  // Head-grouped stream-K plans for causal work were measured on B200 and ran 20-27 %
+  // slower: runs over a pair's first q blocks hold many 2-6 tile units, whose fixed
   // per-unit costs the tile balance does not see.
+  if (table == nullptr || items < 2ll * sms || items > kTableItems || sms > kTableCtas) return p;
+  const long long pair_kv = static_cast<long long>(seq_kv) * 128 * 2 * 2;
+  const int candidates[] = {num_bh, 32, 24, 16, 12, 8, 6, 4, 3, 2, 1};
+  long long best = -1;
+  long long span[11];
+  for (int i = 0; i < 11; ++i) {
+    span[i] = -1;
+    if (candidates[i] > num_bh || (i > 0 && candidates[i] == num_bh)) continue;
+    span[i] = build_table(p, candidates[i], nullptr);
+    if (best < 0 || span[i] < best) best = span[i];
+  }
+  int chosen = num_bh;
+  long long chosen_ws = -1;
+  for (int i = 0; i < 11; ++i) {
+    if (span[i] < 0 || span[i] * 100 > best * 102) continue;
+    const long long ws = candidates[i] * pair_kv;
+    const bool fits = ws <= (48ll << 20);
+    const bool chosen_fits = chosen_ws >= 0 && chosen_ws <= (48ll << 20);
+    if (chosen_ws < 0 || (fits && !chosen_fits) || (fits == chosen_fits && ws < chosen_ws)) {
+      chosen = candidates[i];
+      chosen_ws = ws;
+    }
+  }
+  p.mode = kTable;
+  p.group_pairs = chosen;
+  build_table(p, chosen, table);
   return p;
 }
 
@@ -181,12 +305,14 @@ inline Plan make_plan(int num_bh, int seq_q, int seq_kv, int causal, long long q
 // t1 == t0 == 0): the kernel writes their rows as empty.
 class Walker {
  public:
-  // `p` must outlive the walker (the kernel's parameter block).
-  __host__ __device__ Walker(const Plan& p, int cta) : p_(p), cta_(cta), s_(0), r_(0), pos_(-1), end_(0) {}
+  // `p` (and `t`, kTable's item lists, null for the other plans) must outlive the walker:
+  // in the kernel both are in the parameter block.
+  __host__ __device__ Walker(const Plan& p, int cta, const Table* t = nullptr)
+      : p_(p), t_(t), cta_(cta), s_(0), r_(0), pos_(-1), end_(0) {}
   // Resumes from a state saved with save() (the softmax warps keep it in shared memory
   // across a unit's tile loop rather than in registers).
-  __host__ __device__ Walker(const Plan& p, int cta, int s, int r, int pos, int end)
-      : p_(p), cta_(cta), s_(s), r_(r), pos_(pos), end_(end) {}
+  __host__ __device__ Walker(const Plan& p, int cta, int s, int r, int pos, int end, const Table* t = nullptr)
+      : p_(p), t_(t), cta_(cta), s_(s), r_(r), pos_(pos), end_(end) {}
   __host__ __device__ void save(int* out) const {
     out[0] = s_;
     out[1] = r_;
@@ -195,6 +321,20 @@ class Walker {
   }
 
   __host__ __device__ bool next(Unit& u) {
+    if (p_.mode == kTable) {
+      if (pos_ < 0) {
+        pos_ = t_->start[cta_];
+        end_ = t_->start[cta_ + 1];
+      }
+      if (pos_ >= end_) return false;
+      decode_grouped(p_, t_->item[pos_++], u.bh, u.q0);
+      u.t0 = 0;
+      u.t1 = item_tiles(p_, u.q0);
+      u.kind = kWhole;
+      u.seg = -1;
+      u.cont_lo = u.cont_hi = -1;
+      return true;
+    }
     const int nseg = num_segments(p_);
     while (s_ < nseg) {
       const Segment g = segment(p_, s_);
@@ -250,6 +390,7 @@ class Walker {
 
  private:
   const Plan& p_;
+  const Table* t_;
   int cta_;
   int s_;
   int r_;

@@ -104,7 +104,8 @@ int avo_b200_attn_fwd_ws(const void* q, const void* k, const void* v, void* o, f
  * Diagnostic (no reference counterpart; host only, needs no GPU): the work plan the
  * kernel would run for these sizes on `sm_count` multiprocessors, with (split != 0) or
  * without a workspace.  plan_out[4] = {mode (0 whole items in waves, 1 waves + split
- * tail), CTAs, shortest split run in tiles, items in waves}.  If units and counts are
+ * tail, 2 causal whole items in host-built per-CTA lists over groups of heads), CTAs,
+ * shortest split run in tiles (mode 1) or pairs per group (mode 2), items in waves}.  If units and counts are
  * non-null, CTA c's units go to units[(c * max_units + n) * 8 ...] as
  * {bh, q0, t0, t1, kind (0 whole, 1 first piece, 2 continuation), segment, first and
  * last CTA holding continuation pieces} and counts[c] = its number of units (only the

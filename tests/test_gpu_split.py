@@ -24,8 +24,9 @@ CASES = [
     ((1, 2, 16384, 128), False, 1),    # B1 H16 S16384's shard on one of 8 GPUs
     ((1, 1, 1000, 128), False, 1),     # 4 items of 8 tiles: each in 2 pieces
     ((1, 4, 512, 128), False, 0),      # 8 items of 4 tiles: splitting would not pay
-    ((1, 20, 4096, 128), True, 0),     # causal: whole items, longest first
-    ((1, 160, 1000, 128), True, 0),    # causal with a clipped last block
+    ((1, 20, 4096, 128), True, 2),     # causal: per-CTA lists over groups of heads
+    ((1, 160, 1000, 128), True, 2),    # the same with a clipped last block
+    ((1, 3, 1000, 128), True, 0),      # causal, few items: longest first in waves
 ]
 
 

@@ -9,7 +9,8 @@ walks, so these checks cover what the GPU will do:
 * per CTA and segment at most one continuation piece (its first unit) and one first
   piece (its last unit), so a merging CTA only waits for work its neighbours did at the
   start of their runs, and slots alternate between segments;
-* the runs are balanced, and causal launches keep whole items longest first;
+* the runs are balanced; causal launches with many items use per-CTA lists over groups of
+  heads (balanced like longest-first waves, with few pairs in flight);
 * the flag protocol on the slots (writer waits for 0, sets 1; merger waits for 1,
   resets to 0) ends under random CTA speeds and never hands a merger another item's
   piece.
@@ -103,17 +104,30 @@ def test_split_plans_balance_the_ctas(b200, num_bh, seq, causal, bound):
     assert max(tiles) <= bound * total / 148 + 2, (max(tiles), total / 148)
 
 
-@pytest.mark.parametrize("split", [False, True])
-def test_causal_keeps_the_balanced_wave_order(b200, split):
-    # causal: longest query blocks first over all heads, waves in alternating directions,
-    # with or without a workspace (within ~2 % of the mean tile count per CTA)
-    mode, grid, _, _, units = b200.schedule_units(32, 8192, 8192, True, split=split)
-    assert mode == 0 and grid == 148
+@pytest.mark.parametrize("num_bh,seq,group,pairs_bound", [(32, 8192, 8, 16), (16, 32768, 2, 8), (16, 16384, 4, 8)])
+def test_causal_table_plan_is_balanced_and_l2_local(b200, num_bh, seq, group, pairs_bound):
+    # causal, many items, with a workspace: whole items in host-built per-CTA lists over
+    # groups of pairs (mode 2), as balanced as longest-first waves, with far fewer pairs in
+    # flight; without a workspace the launch keeps the waves (mode 0)
+    assert b200.schedule_units(num_bh, seq, seq, True, split=False)[0] == 0
+    mode, grid, g, _, units = b200.schedule_units(num_bh, seq, seq, True, split=True, max_units=4096)
+    assert mode == 2 and grid == 148 and g == group
     tiles = [sum(u[3] - u[2] for u in us) for us in units]
     assert max(tiles) <= 1.02 * sum(tiles) / grid
-    first_wave = [units[c][0][:2] for c in range(grid)]
-    assert first_wave[0] == [0, 31 * 256] and first_wave[31] == [31, 31 * 256] and first_wave[32] == [0, 30 * 256]
-    assert units[147][1][:2] == [(148 + 0) % 32, (31 - 148 // 32) * 256]
+    depth = max(len(us) for us in units)
+    in_flight = max(len({us[k][0] for us in units if len(us) > k}) for k in range(depth))
+    assert in_flight <= pairs_bound < num_bh
+    # every CTA's list runs through the groups in order
+    for us in units:
+        groups = [u[0] // g for u in us]
+        assert groups == sorted(groups)
+
+
+def test_causal_few_items_keep_the_wave_order(b200):
+    # fewer than two items per SM: longest query blocks first over all heads, in waves
+    mode, grid, _, _, units = b200.schedule_units(3, 1000, 1000, True)
+    assert mode == 0
+    assert [u[:2] for u in units[0]] == [[0, 768]]
 
 
 def simulate_flags(units, seed):
