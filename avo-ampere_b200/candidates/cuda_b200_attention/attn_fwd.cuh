@@ -292,29 +292,39 @@ __device__ __forceinline__ float exp_half_max(const uint32_t (&s)[4][32], uint64
   return fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
 }
 
-// Flag of a split-piece slot: poll with acquire semantics until it holds `want`, bounded
-// by the watchdog.  One lane polls; the warp then proceeds together.
-__device__ __forceinline__ bool wait_flag(const int* flag, int want, const Watch& w) {
+// Flags of split-piece slots (cta_lo..cta_hi, parity, tile): poll with acquire semantics
+// until each holds `want`, bounded by the watchdog.  Lane k polls CTAs cta_lo + k,
+// cta_lo + k + 32, ..., so the polls of all pieces are in flight together.
+__device__ __forceinline__ bool wait_flags(const int* flags, int cta_lo, int cta_hi, int parity, int tile, int want,
+                                           const Watch& w) {
   bool ok = true;
-  if ((threadIdx.x & 31) == 0) {
-    if (ld_acquire_gpu(flag) != want) {
-      const uint64_t t0 = global_timer_ns();
-      while (true) {
-        if (ld_acquire_gpu(flag) == want) break;
-        if (*w.abort) { ok = false; break; }
-        if (global_timer_ns() - t0 > w.limit_ns) {
-          *w.abort = 1;
-          if (w.status != nullptr) atomicOr(w.status, kStatusWatchdog);
-          ok = false;
-          break;
-        }
-        __nanosleep(64);
+  for (int c = cta_lo + static_cast<int>(threadIdx.x & 31); ok && c <= cta_hi; c += 32) {
+    const int* flag = flags + slot_index(c, parity, tile);
+    if (ld_acquire_gpu(flag) == want) continue;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+      if (ld_acquire_gpu(flag) == want) break;
+      if (*w.abort) { ok = false; break; }
+      if (global_timer_ns() - t0 > w.limit_ns) {
+        *w.abort = 1;
+        if (w.status != nullptr) atomicOr(w.status, kStatusWatchdog);
+        ok = false;
+        break;
       }
+      __nanosleep(64);
     }
   }
-  const bool all = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-  __threadfence();  // every lane's later reads of the slot are ordered after lane 0's acquire
+  const bool all = __all_sync(0xffffffffu, ok);
+  __threadfence();  // every lane's later reads of the slots are ordered after the acquires
   return all;
+}
+
+// Online merge of a continuation piece's row (max mc, sum lc) into (m, l), log2 units.
+__device__ __forceinline__ void merge_ml(float& m, float& l, float mc, float lc) {
+  if (mc == -CUDART_INF_F || !(lc > 0.f)) return;
+  const float mn = fmaxf(m, mc);
+  l = (m == -CUDART_INF_F ? 0.f : l * ex2_approx(m - mn)) + lc * ex2_approx(mc - mn);
+  m = mn;
 }
 
 // Persistent: each CTA walks its unit sequence (schedule.cuh).  Every role walks the same
@@ -574,10 +584,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar_sync(kBarPHalf + 2 * i + 1, kPHalfThreads);
       }
 
-      if (ok && n_tiles > 0) {
-        ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (ph >> 1) & 1u, watch));
-        tc_fence_after();
-      }
 
       // Epilogue.  A whole item: O / l -> bf16 -> this thread's output row, written
       // straight from registers as 8 whole 32-byte sectors (16-byte stores when o or its
@@ -596,30 +602,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       u.seg = wst[9];
       u.cont_lo = wst[10];
       u.cont_hi = wst[11];
-      const bool have = ok && n_tiles > 0;
       const int parity = u.seg & 1;
+      // The slot flags are polled before the wait for O (both only wait; the flag polls
+      // are L2 round trips that then overlap the last PV): a first piece needs every
+      // continuation piece's slot full, a continuation piece needs its own slot free.
+      if (u.kind == sched::kFirst) {
+        ok = wait_flags(p.part_flag, u.cont_lo, u.cont_hi, parity, i, 1, watch) && ok;
+      } else if (u.kind == sched::kCont) {
+        ok = wait_flags(p.part_flag, blockIdx.x, blockIdx.x, parity, i, 0, watch) && ok;
+      }
+      if (ok && n_tiles > 0) {
+        ok = __all_sync(0xffffffffu, wait_phase(bar(BAR_O_DONE + i), (ph >> 1) & 1u, watch));
+        tc_fence_after();
+      }
+      const bool have = ok && n_tiles > 0;
       const int row = u.q0 + i * kBlockM + t;
       const bool write = row < p.seq_q && *abort_flag == 0;
       float m_fin = (have && l > 0.f) ? m : -CUDART_INF_F;
       float l_fin = m_fin == -CUDART_INF_F ? 0.f : l;
       float f_own = 1.f;
-      if (u.kind == sched::kFirst) {
-        for (int c = u.cont_lo; c <= u.cont_hi; ++c) {
-          const long long sl = slot_index(c, parity, i);
-          ok = wait_flag(p.part_flag + sl, 1, watch) && ok;
-          if (ok) m_fin = fmaxf(m_fin, __ldcg(p.part_ml + sl * kSlotMl + t));
+      if (u.kind == sched::kFirst && ok) {
+        // (m, l) of all pieces merged online, two pieces' loads in flight at a time.
+        for (int c = u.cont_lo; c <= u.cont_hi; c += 2) {
+          const float* mla = p.part_ml + slot_index(c, parity, i) * kSlotMl;
+          const float* mlb = p.part_ml + slot_index(c < u.cont_hi ? c + 1 : c, parity, i) * kSlotMl;
+          const float ma = __ldcg(mla + t), la = __ldcg(mla + kBlockM + t);
+          const float mb = __ldcg(mlb + t), lb = __ldcg(mlb + kBlockM + t);
+          merge_ml(m_fin, l_fin, ma, la);
+          if (c < u.cont_hi) merge_ml(m_fin, l_fin, mb, lb);
         }
-        f_own = (m_fin == -CUDART_INF_F || !(l_fin > 0.f)) ? 0.f : ex2_approx(m - m_fin);
-        l_fin *= f_own;
-        if (ok) {
-          for (int c = u.cont_lo; c <= u.cont_hi; ++c) {
-            const long long sl = slot_index(c, parity, i);
-            const float mc = __ldcg(p.part_ml + sl * kSlotMl + t);
-            if (mc != -CUDART_INF_F) l_fin += __ldcg(p.part_ml + sl * kSlotMl + kBlockM + t) * ex2_approx(mc - m_fin);
-          }
-        }
-      } else if (u.kind == sched::kCont) {
-        ok = wait_flag(p.part_flag + slot_index(blockIdx.x, parity, i), 0, watch) && ok;
+        f_own = (!(have && l > 0.f) || m_fin == -CUDART_INF_F) ? 0.f : ex2_approx(m - m_fin);
       }
       const bool seen = (m_fin != -CUDART_INF_F) && (l_fin > 0.f);
       const float inv_l = seen ? 1.f / l_fin : 0.f;
@@ -677,24 +689,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (ok) {
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] = f2u(u2f(o[e]) * f_own);
-            for (int cc = u.cont_lo; cc <= u.cont_hi; ++cc) {
-              const long long sl = slot_index(cc, parity, i);
-              const float mc = __ldcg(p.part_ml + sl * kSlotMl + t);
-              if (mc == -CUDART_INF_F) continue;
-              const float fc = ex2_approx(mc - m_fin);
-              const float4* src = reinterpret_cast<const float4*>(p.part_o + sl * kSlotO);
+            // Two pieces per round trip: each piece's row max and its 32 partial values
+            // are loaded together, with no branch between them (a piece whose row saw no
+            // key gets factor 0; its slot still holds finite values, zeros).  An odd last
+            // piece loads only its own slot (zeros stand in for the second).
+            for (int cc = u.cont_lo; cc <= u.cont_hi; cc += 2) {
+              const bool two = cc < u.cont_hi;
+              const long long sa = slot_index(cc, parity, i);
+              const long long sb = slot_index(two ? cc + 1 : cc, parity, i);
+              const float ma = __ldcg(p.part_ml + sa * kSlotMl + t);
+              const float mb = __ldcg(p.part_ml + sb * kSlotMl + t);
+              const float4* src_a = reinterpret_cast<const float4*>(p.part_o + sa * kSlotO);
+              const float4* src_b = reinterpret_cast<const float4*>(p.part_o + sb * kSlotO);
+              float4 va[8], vb[8];
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const float4 a = __ldcg(src + ((c * 4 + q) * kBlockM + t) * 2);
-                const float4 b = __ldcg(src + ((c * 4 + q) * kBlockM + t) * 2 + 1);
-                o[8 * q + 0] = f2u(fmaf(a.x, fc, u2f(o[8 * q + 0])));
-                o[8 * q + 1] = f2u(fmaf(a.y, fc, u2f(o[8 * q + 1])));
-                o[8 * q + 2] = f2u(fmaf(a.z, fc, u2f(o[8 * q + 2])));
-                o[8 * q + 3] = f2u(fmaf(a.w, fc, u2f(o[8 * q + 3])));
-                o[8 * q + 4] = f2u(fmaf(b.x, fc, u2f(o[8 * q + 4])));
-                o[8 * q + 5] = f2u(fmaf(b.y, fc, u2f(o[8 * q + 5])));
-                o[8 * q + 6] = f2u(fmaf(b.z, fc, u2f(o[8 * q + 6])));
-                o[8 * q + 7] = f2u(fmaf(b.w, fc, u2f(o[8 * q + 7])));
+              for (int q = 0; q < 8; ++q) {
+                va[q] = __ldcg(src_a + ((c * 4 + (q >> 1)) * kBlockM + t) * 2 + (q & 1));
+                vb[q] = two ? __ldcg(src_b + ((c * 4 + (q >> 1)) * kBlockM + t) * 2 + (q & 1))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+              const float fa = ma == -CUDART_INF_F ? 0.f : ex2_approx(ma - m_fin);
+              const float fb = (!two || mb == -CUDART_INF_F) ? 0.f : ex2_approx(mb - m_fin);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                o[4 * q + 0] = f2u(fmaf(vb[q].x, fb, fmaf(va[q].x, fa, u2f(o[4 * q + 0]))));
+                o[4 * q + 1] = f2u(fmaf(vb[q].y, fb, fmaf(va[q].y, fa, u2f(o[4 * q + 1]))));
+                o[4 * q + 2] = f2u(fmaf(vb[q].z, fb, fmaf(va[q].z, fa, u2f(o[4 * q + 2]))));
+                o[4 * q + 3] = f2u(fmaf(vb[q].w, fb, fmaf(va[q].w, fa, u2f(o[4 * q + 3]))));
               }
             }
           }
