@@ -137,6 +137,36 @@ def _stream_handle(device) -> int:
     return _torch().cuda.current_stream(device).cuda_stream
 
 
+_raw_stream_getter: Any = None
+
+
+def _raw_stream(index: int) -> int:
+    """The current stream of device ``index`` as a cudaStream_t value.  torch's own raw
+    getter costs ~0.1 us against ~3 us for building a Stream object; the public API is
+    the fallback where the getter is absent."""
+    global _raw_stream_getter
+    if _raw_stream_getter is None:
+        torch = _torch()
+        getter = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+        _raw_stream_getter = getter if getter is not None else (
+            lambda i: torch.cuda.current_stream(i).cuda_stream)
+    return _raw_stream_getter(index)
+
+
+_launch_states: dict[int, tuple[int, int, int]] = {}
+
+
+def _launch_state(index: int) -> tuple[int, int, int]:
+    """(workspace address, workspace bytes, status word address) of device ``index``,
+    looked up once per device (both buffers live for the life of the process)."""
+    state = _launch_states.get(index)
+    if state is None:
+        ws = workspace(index)
+        state = (ws.data_ptr(), ws.numel(), status_word(index).data_ptr())
+        _launch_states[index] = state
+    return state
+
+
 def status_word(device) -> Any:
     """Per-device int32 word that kernels OR their watchdog bits into."""
     torch = _torch()
@@ -189,6 +219,14 @@ def check_status(device, *, reset: bool = True) -> int:
 
 def _validate(q, k, v) -> None:
     torch = _torch()
+    # The common, valid case in one pass of cheap attribute reads; any failure falls
+    # through to the checks below, which raise what the reference binding would.
+    if q.is_cuda and k.is_cuda and v.is_cuda and q.is_contiguous() and k.is_contiguous() and v.is_contiguous():
+        shape = q.shape
+        bf16 = torch.bfloat16
+        if (shape == k.shape and shape == v.shape and len(shape) == 4 and q.dtype is bf16 and k.dtype is bf16
+                and v.dtype is bf16 and shape[3] == HEAD_DIM and q.get_device() == k.get_device() == v.get_device()):
+            return
     # Same checks, same order, as the reference binding (attention.cpp:13-21).
     for name, t in (("q", q), ("k", k), ("v", v)):
         if not t.is_cuda:
@@ -225,7 +263,7 @@ def attention_forward(q, k, v, causal: bool, *, softmax_scale: float | None = No
     only."""
     torch = _torch()
     _validate(q, k, v)
-    batch, heads, seq, head_dim = (int(x) for x in q.shape)
+    batch, heads, seq, head_dim = q.shape
     if out is None:
         out = torch.empty_like(q)
     if need_lse and lse is None:
@@ -233,23 +271,29 @@ def attention_forward(q, k, v, causal: bool, *, softmax_scale: float | None = No
     if not need_lse:
         lse = None
     scale = default_scale(head_dim) if softmax_scale is None else float(softmax_scale)
-    lib = load_library()
-    with torch.cuda.device(q.device):
+    lib = _lib if _lib is not None else load_library()
+    # The call costs a few microseconds of host time, which is what small problems are
+    # bound by: per-device state is cached, the raw current stream is read directly, and
+    # the device is switched only when q is not on the current one.
+    index = q.get_device()
+    ws_ptr, ws_bytes, status_ptr = _launch_state(index)
+    lse_ptr = lse.data_ptr() if lse is not None else None
+
+    def call() -> int:
         if split:
-            ws = workspace(q.device)
-            code = lib.avo_b200_attn_fwd_ws(
-                q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
-                lse.data_ptr() if lse is not None else None,
-                batch, heads, seq, head_dim, 1 if causal else 0, scale, ws.data_ptr(), ws.numel(),
-                status_word(q.device).data_ptr(), _stream_handle(q.device),
-            )
-        else:
-            code = lib.avo_b200_attn_fwd(
-                q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
-                lse.data_ptr() if lse is not None else None,
-                batch, heads, seq, head_dim, 1 if causal else 0, scale,
-                status_word(q.device).data_ptr(), _stream_handle(q.device),
-            )
+            return lib.avo_b200_attn_fwd_ws(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse_ptr,
+                batch, heads, seq, head_dim, 1 if causal else 0, scale, ws_ptr, ws_bytes,
+                status_ptr, _raw_stream(index))
+        return lib.avo_b200_attn_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse_ptr,
+            batch, heads, seq, head_dim, 1 if causal else 0, scale, status_ptr, _raw_stream(index))
+
+    if index == torch.cuda.current_device():
+        code = call()
+    else:
+        with torch.cuda.device(index):
+            code = call()
     _check(code, "avo_b200_attn_fwd_ws" if split else "avo_b200_attn_fwd")
     return out, lse
 
