@@ -20,7 +20,7 @@
 //   * warps 0-3 and 4-7 are two softmax warpgroups, one per Q tile, one thread
 //     per query row: tcgen05.ld of the S row, max, exp2 with scale*log2(e) folded
 //     into one FFMA, row sum, tcgen05.st of P.  The running max is only raised
-//     when it grows by more than 2^8 ("conditional rescale"), so O in TMEM is
+//     when it grows by more than 2^15 ("conditional rescale"), so O in TMEM is
 //     rescaled rarely; the two groups ping-pong against the tensor core;
 //   * causal tiles above the diagonal are never loaded or multiplied;
 //   * the epilogue scales O by 1/l and writes each row straight from registers as
@@ -78,7 +78,13 @@ constexpr uint32_t kRegsSoftmax = 216;
 constexpr uint32_t kRegsOther = 72;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunch, "register split");
 constexpr uint32_t kTmemCols = 512;            // S0 | S1 | O0 | O1, 128 columns each
-constexpr float kRescaleThreshold = 8.0f;      // log2 units: rescale only past 2^8 growth
+// log2 units: the running max (and O, l with it) moves only when a tile's max exceeds it by
+// more than 2^15, so P = 2^(s*scale - m) stays below 2^15: exact in bf16 (8 exponent bits),
+// inside the FMA-pipe exp2's input range, and the fp32 O accumulator could only overflow for
+// |V| above ~1e28.  Measured on B200 with k x3 (B1 H16 S16384): at 2^8, 4.2 % of warp-tiles
+// after the first took the rescale path and, as a group's P hand-off waits for all four of
+// its warps, ~16 % of group-tiles stalled on it (+15 % cycles per launch); at 2^15, none.
+constexpr float kRescaleThreshold = 15.0f;
 // FMA-pipe exp2 share: 1 of every 8 pairs (measured on B200: 1/8 beat 0/8 by 4-7 % and
 // 3/8 by ~4 %; 2/8 is within noise of it).
 constexpr int kEmuPairsPer8 = 1;
@@ -488,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
         // Speculative P for keys 0-63 against the running max, computed side by side
         // with the row max over all 128 scores (independent instruction streams).  The
-        // running max only moves when the tile max exceeds it by more than 2^8, so the
+        // running max only moves when the tile max exceeds it by more than 2^15, so the
         // speculation almost always stands; when it does not (first tile, rare jumps)
         // the half is recomputed with the new max, giving exactly the values a
         // max-first order would.  An overflow of the speculative exp2 implies a move.

@@ -78,6 +78,33 @@ def test_k_scaled_x3_stresses_rescale(b200, causal):
 
 
 @pytest.mark.parametrize("causal", [False, True])
+def test_growing_scores_force_rescales(b200, causal):
+    # Keys scaled from x1 to x5 along the sequence: a row's max grows by ~20 (log2 units)
+    # over its tiles, past the kernel's 2^15 rescale threshold, so the rescale path (P
+    # recomputed against the new max, O and l scaled in place) runs on later tiles (on
+    # ~37 % of the non-causal and ~7 % of the causal warp-tiles after the first, by a
+    # host simulation of the same inputs).  Steeper ramps make the softmax so peaked that
+    # bf16 rounding of P alone reaches the 2e-2 bound, whatever the threshold.
+    import torch
+
+    from avo.benchmark import fp32_reference
+
+    shape = (1, 2, 2048, 128)
+    q, k, v = oracle.make_inputs(shape, seed=13)
+    ramp = torch.linspace(1.0, 5.0, shape[2]).view(1, 1, -1, 1)
+    k = (k.float() * ramp).to(torch.bfloat16)
+    dq, dk, dv = (t.cuda() for t in (q, k, v))
+    out, lse = b200.attention_forward(dq, dk, dv, causal)
+    torch.cuda.synchronize()
+    b200.check_status(dq.device)
+    ref_o, ref_lse = fp32_reference(dq, dk, dv, causal)
+    diff = (out.float() - ref_o).abs()
+    assert diff.max().item() <= oracle.MAX_ABS_TOL, diff.max().item()
+    assert diff.mean().item() <= oracle.MEAN_ABS_TOL, diff.mean().item()
+    assert (lse - ref_lse).abs().max().item() <= oracle.LSE_TOL
+
+
+@pytest.mark.parametrize("causal", [False, True])
 def test_s4096_two_heads(b200, causal):
     inputs, out, lse = _run(b200, (1, 2, 4096, 128), causal, seed=11)
     _check(inputs, out, lse, causal)

@@ -58,7 +58,7 @@ def test_online_recurrences_match_reference_seed(name):
     q, k, v = _inputs(name)
     heads = entry["o_fp32_heads"]
     golden = ARRAYS[f"{name}/o_fp32"]
-    for threshold in (None, 8.0):
+    for threshold in (None, 8.0, 15.0):
         o, _ = oracle.attention_online(q, k, v, entry["causal"], block=128, rescale_threshold=threshold)
         assert np.abs(o[:, :heads] - golden).max() <= 2e-5
 
