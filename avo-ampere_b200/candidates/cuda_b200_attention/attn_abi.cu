@@ -117,6 +117,7 @@ std::mutex g_mu;
 EncodeTiledFn g_encode = nullptr;
 int g_device_state[kMaxDevices] = {};  // 0 unchecked, 1 ready, -1 not a B200
 int g_sm_count[kMaxDevices] = {};      // multiprocessors, read once per device
+int g_coop[kMaxDevices] = {};          // cooperative launch supported, read once per device
 
 // Pipeline-wait limit (AVO_B200_WATCHDOG_MS, default 2 s).  It is wall-clock time
 // (%globaltimer): on a GPU time-sliced between contexts (another process's work scheduled
@@ -207,8 +208,14 @@ int prepare_device(int* sm_count = nullptr) {
     (void)cudaGetLastError();
     return AVO_B200_ENODEV;
   }
+  int coop = 0;
+  if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    coop = 0;
+  }
   if (dev < kMaxDevices) {
     g_sm_count[dev] = sms;
+    g_coop[dev] = coop != 0 ? 1 : 0;
     g_device_state[dev] = 1;
   }
   if (sm_count != nullptr) *sm_count = sms;
@@ -220,6 +227,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // Whether the current device supports cooperative launches (all CTAs resident at once).
 bool cooperative_ok() {
   int dev = -1, coop = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices && g_device_state[dev] == 1)
+    return g_coop[dev] != 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess) {
     (void)cudaGetLastError();
@@ -292,7 +301,9 @@ const PlanEntry& cached_plan(int num_bh, int seq_q, int seq_kv, int causal, long
     bool same = true;
     for (int i = 0; i < 8; ++i) same = same && g_plans[e].key[i] == key[i];
     if (same) {
-      mine = g_plans[e];
+      // The 25 KB table is copied only for the plan that launches with it.
+      mine.plan = g_plans[e].plan;
+      if (mine.plan.mode == sched::kTable) mine.table = g_plans[e].table;
       return mine;
     }
   }
@@ -371,8 +382,26 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
 
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (plan.mode == sched::kWaves) {
-    attn_fwd_kernel<false><<<static_cast<unsigned>(grid), kThreads, kSmemBytes, st>>>(tm_q, tm_k, tm_v, p,
-                                                                                       TableParam<false>{0});
+    // Programmatic dependent launch: this launch's CTAs may start their set-up on free
+    // multiprocessors while the previous work in the stream finishes (the kernel waits for
+    // it before touching global memory).  Measured on B200: ~1.3 us less per back-to-back
+    // launch of small problems.  The table plan keeps plain ordering (it measured 2 % more
+    // cycles with it: two 25 KB parameter blocks then compete in the constant cache), as
+    // does the split plan's cooperative launch.
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, attn_fwd_kernel<false>, tm_q, tm_k, tm_v, p, TableParam<false>{0}) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return AVO_B200_ELAUNCH;
+    }
   } else if (plan.mode == sched::kTable) {
     attn_fwd_kernel<true><<<static_cast<unsigned>(grid), kThreads, kSmemBytes, st>>>(tm_q, tm_k, tm_v, p,
                                                                                       entry.table);

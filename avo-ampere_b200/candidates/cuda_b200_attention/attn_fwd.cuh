@@ -397,6 +397,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Everything above touches only this CTA's shared memory, TMEM and the parameter block,
+  // so it may overlap the previous launch in the stream when the launch allows it; every
+  // global-memory access below (the Q/K/V loads, O/LSE stores, status word, workspace)
+  // comes after the wait.  The next launch may then start its own set-up on free
+  // multiprocessors: this grid is persistent, at most one CTA per multiprocessor, all
+  // resident from the start, so nothing of it waits for a multiprocessor.
+  grid_dependency_wait();
+  grid_launch_dependents();
 
   const uint32_t sQ = sbase + kSmemQ;
   const uint32_t sRing = sbase + kSmemRing;

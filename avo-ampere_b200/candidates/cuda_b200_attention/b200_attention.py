@@ -75,6 +75,10 @@ class B200AttentionError(RuntimeError):
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
+# The per-call entry avo_b200_attn_fwd_ws through the CPython binding in fast_call.c (bound
+# to the address of the same function in the loaded library), or None where that binding
+# was not built: the ctypes call is then used.
+_fwd_ws_fast: Any = None
 _status_words: dict[int, Any] = {}
 _workspaces: dict[int, Any] = {}
 
@@ -114,8 +118,21 @@ def load_library(*, build: bool = True) -> ctypes.CDLL:
         version = lib.avo_b200_abi_version()
         if version != ABI_VERSION:
             raise B200AttentionError(f"ABI version {version} != expected {ABI_VERSION}")
+        _bind_fast(builder, lib)
         _lib = lib
         return lib
+
+
+def _bind_fast(builder, lib: ctypes.CDLL) -> None:
+    global _fwd_ws_fast
+    path = getattr(builder, "FAST_PATH", None)
+    if path is None or not path.is_file():
+        return
+    spec = importlib.util.spec_from_file_location("_avo_b200_fast", path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    module.bind(ctypes.cast(lib.avo_b200_attn_fwd_ws, ctypes.c_void_p).value)
+    _fwd_ws_fast = module.fwd_ws
 
 
 def strerror(code: int) -> str:
@@ -281,7 +298,7 @@ def attention_forward(q, k, v, causal: bool, *, softmax_scale: float | None = No
 
     def call() -> int:
         if split:
-            return lib.avo_b200_attn_fwd_ws(
+            return (_fwd_ws_fast or lib.avo_b200_attn_fwd_ws)(
                 q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse_ptr,
                 batch, heads, seq, head_dim, 1 if causal else 0, scale, ws_ptr, ws_bytes,
                 status_ptr, _raw_stream(index))

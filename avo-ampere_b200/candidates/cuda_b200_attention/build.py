@@ -16,6 +16,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 import tempfile
 from pathlib import Path
 
@@ -36,8 +37,37 @@ NVCC_FLAGS = (
 )
 
 
+FAST_SOURCE = HERE / "fast_call.c"
+FAST_PATH = HERE / ("_avo_b200_fast" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+
+
 class BuildError(RuntimeError):
     """nvcc failed or could not be found."""
+
+
+def build_fast(*, force: bool = False) -> Path | None:
+    """Compile the CPython binding of the per-call entry (fast_call.c) with the host C
+    compiler, if it is missing or older than its source.  Returns its path, or None when
+    no compiler or no Python headers are available (the ctypes binding is then used)."""
+    if not force and FAST_PATH.is_file() and FAST_PATH.stat().st_mtime >= FAST_SOURCE.stat().st_mtime:
+        return FAST_PATH
+    compiler = shutil.which(os.environ.get("CC", "") or "gcc") or shutil.which("cc")
+    include = sysconfig.get_paths().get("include")
+    if compiler is None or not include or not (Path(include) / "Python.h").is_file():
+        return None
+    fd, tmp_name = tempfile.mkstemp(prefix="._avo_b200_fast.", suffix=".so", dir=HERE)
+    os.close(fd)
+    tmp = Path(tmp_name)
+    try:
+        command = [compiler, "-O2", "-shared", "-fPIC", "-I", include, str(FAST_SOURCE), "-o", str(tmp)]
+        completed = subprocess.run(command, text=True, capture_output=True, check=False)
+        if completed.returncode != 0:
+            raise BuildError(f"{' '.join(command)} failed:\n{completed.stderr[-2000:]}")
+        os.replace(tmp, FAST_PATH)
+    finally:
+        if tmp.exists():
+            tmp.unlink()
+    return FAST_PATH
 
 
 def include_dir() -> Path:
@@ -91,7 +121,9 @@ def build_command(output: Path, *, ptxas_verbose: bool = False) -> list[str]:
 
 
 def build(*, force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> Path:
-    """Compile the library if it is missing or older than its sources; return its path."""
+    """Compile the library (and the CPython binding of its per-call entry) if missing or
+    older than their sources; return the library's path."""
+    build_fast(force=force)
     if not force and not needs_build():
         return LIB_PATH
     fd, tmp_name = tempfile.mkstemp(prefix=".libavo_b200_attn.", suffix=".so", dir=HERE)

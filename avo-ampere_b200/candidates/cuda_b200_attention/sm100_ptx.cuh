@@ -66,6 +66,15 @@ __device__ __forceinline__ uint32_t mbar_try_wait_sleep(uint32_t bar, uint32_t p
 }
 
 // ---------------------------------------------------------------- TMA
+// Programmatic dependent launch.  wait: blocks until every grid this one depends on in
+// its stream has completed and its memory operations are visible (a no-op when the launch
+// did not allow early start).  launch_dependents: lets the next such launch in the stream
+// start its CTAs on free multiprocessors before this grid ends.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

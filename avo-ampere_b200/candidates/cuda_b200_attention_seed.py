@@ -29,6 +29,7 @@ AVO_SOURCE_FILES = (
     "cuda_b200_attention/schedule.cuh",
     "cuda_b200_attention/attn_fwd.cuh",
     "cuda_b200_attention/attn_abi.cu",
+    "cuda_b200_attention/fast_call.c",
     "cuda_b200_attention/b200_attention.py",
     "cuda_b200_attention/build.py",
 )
