@@ -108,3 +108,25 @@ def test_build_flags_target_sm100a():
     command = build.build_command(Path("/tmp/x.so"))
     assert "arch=compute_100a,code=sm_100a" in command
     assert "-shared" in command and "-lineinfo" in command
+
+
+def test_cpython_binding_builds_and_checks_arguments():
+    # The per-call entry's CPython binding (fast_call.c) compiles with the host compiler and
+    # refuses a wrong argument count before it touches the library (no GPU needed).
+    import importlib.util
+    import sys
+    from pathlib import Path
+
+    here = Path(__file__).resolve().parents[1] / "avo-ampere_b200" / "candidates" / "cuda_b200_attention"
+    spec = importlib.util.spec_from_file_location("avo_b200_build_for_test", here / "build.py")
+    builder = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(builder)
+    path = builder.build_fast()
+    if path is None:
+        pytest.skip("no C compiler or Python headers")
+    spec = importlib.util.spec_from_file_location("_avo_b200_fast", path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    with pytest.raises(TypeError):
+        module.fwd_ws(1, 2, 3)
+    assert sys.modules.get("avo_b200_build_for_test") is None
